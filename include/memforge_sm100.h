@@ -1,0 +1,186 @@
+/*
+ * memforge_sm100.h — C ABI of the B200 (sm_100a) paged-attention library.
+ *
+ * This library replaces the KV-scatter and paged-attention hot path of
+ * MemForge (reference paths below are relative to the MemForge source tree).
+ * Every entry point:
+ *   - takes plain device pointers, element strides and sizes (no framework types);
+ *   - is stream-ordered on `stream` (NULL = the legacy default stream) and never
+ *     synchronises the device or allocates device memory;
+ *   - returns 0 on success or a negative MF_E* code; `mf_last_error()` then
+ *     gives a message (per calling thread);
+ *   - optionally reports device-side violations (a bad block id, a slot past the
+ *     pool, a bounded wait that gave up) by OR-ing MF_ERR_* bits into `*err_flag`
+ *     (a device int32 the caller zeroes and reads back when it wants to check).
+ *     Such a launch never traps: the offending access is skipped or clamped.
+ *
+ * Pool addressing (one layer): element (slot s, kv head h, dim d) lives at
+ *   base + (s / block_size) * stride_block + (s % block_size) * stride_slot
+ *        + h * stride_head + d
+ * which covers MemForge's pool layer `(blocks, block_size, kv_heads, head_dim)`
+ * (memforge_ml/runtime/kv_pool.py:66) and the standalone operator's cache
+ * `(blocks, heads, block_size, head_dim)` (memforge_ml/models/paged_attention.py:34-43).
+ */
+#ifndef MEMFORGE_SM100_H
+#define MEMFORGE_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MF_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MF_API __attribute__((visibility("default")))
+#else
+#define MF_API
+#endif
+
+/* Same object as cudaStream_t. */
+typedef struct CUstream_st* mf_stream_t;
+
+typedef enum { MF_F32 = 0, MF_F16 = 1, MF_BF16 = 2 } mf_dtype;
+
+enum {
+  MF_OK = 0,
+  MF_EINVAL = -1,        /* bad argument: null pointer, shape, stride, dtype */
+  MF_EBOUNDS = -2,       /* host-visible bound violation */
+  MF_ETIMEOUT = -3,      /* reserved: a bounded wait gave up (also MF_ERR_TIMEOUT) */
+  MF_ECUDA = -4,         /* CUDA runtime error while launching */
+  MF_EUNSUPPORTED = -5,  /* no kernel in this build handles the shape */
+  MF_EWORKSPACE = -6     /* workspace missing or too small */
+};
+
+/* Bits OR-ed into *err_flag by kernels. */
+#define MF_ERR_BLOCK_ID 0x1  /* block table entry outside [0, num_blocks) */
+#define MF_ERR_SLOT 0x2      /* slot_mapping entry outside [-1, num_blocks*block_size) */
+#define MF_ERR_TABLE 0x4     /* a context needs more blocks than the table row holds */
+#define MF_ERR_LENGTH 0x8    /* kv_len < q_len, or a query row with no visible key */
+#define MF_ERR_TIMEOUT 0x10  /* a bounded pipeline wait gave up */
+
+MF_API int mf_abi_version(void);
+MF_API const char* mf_last_error(void);
+
+/* Number of multiprocessors and whether the device is sm_100 (1) or not (0). */
+MF_API int mf_device_info(int device, int* num_sms, int* is_sm100);
+
+/*
+ * reshape_and_cache — scatter new K/V rows into the paged pool.
+ *
+ * Replaces paged_gather.scatter_kv (memforge_ml/kernels/paged_gather.py:92-117)
+ * and PagedKVPool.write_flat / write (memforge_ml/runtime/kv_pool.py:134-149,
+ * 181-192): token t, head h of `key`/`value` (element (t, h, d) at
+ * key + t*k_stride_tok + h*k_stride_head + d) lands at pool slot
+ * slot_mapping[t].  A slot of -1 skips the token (padding).  When src_dtype
+ * differs from pool_dtype the values are rounded to the pool dtype exactly as
+ * torch's `.to()` does (round to nearest even; NaN -> the canonical NaN).
+ * Supported (src, pool): (f32,f32) (f16,f16) (bf16,bf16) (f32,bf16) (f32,f16).
+ * Two tokens naming one slot race (the reference rejects that case,
+ * memforge_ml/runtime/varlen_cache.py:186-190).
+ */
+MF_API int mf_reshape_and_cache(const void* key, const void* value, mf_dtype src_dtype,
+                         int64_t k_stride_tok, int64_t k_stride_head,
+                         int64_t v_stride_tok, int64_t v_stride_head,
+                         void* key_pool, void* value_pool, mf_dtype pool_dtype,
+                         int64_t pool_stride_block, int64_t pool_stride_slot,
+                         int64_t pool_stride_head, int32_t num_blocks, int32_t block_size,
+                         const void* slot_mapping, int32_t slot_mapping_is_int64,
+                         int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t* err_flag, mf_stream_t stream);
+
+/*
+ * Paged attention over block tables: decode, speculative verify and varlen
+ * chunked prefill in one contract.
+ *
+ * Sequence s owns query rows [q_start(s), q_start(s) + q_len(s)) where
+ * q_start/q_len come from cu_seqlens_q[s..s+1] (or s*q_per_seq / q_per_seq when
+ * cu_seqlens_q is NULL).  kv_lens[s] is the number of keys visible to its LAST
+ * query row.  With causal != 0, row i (0-based within the sequence) attends to
+ * key positions 0 .. kv_lens[s] - q_len(s) + i; with causal == 0 every row
+ * attends to 0 .. kv_lens[s] - 1.  Key position p of sequence s is pool slot
+ * block_tables[s*table_stride + p/block_size]*block_size + p%block_size, except
+ * that, when win_k/win_v are given, positions kv_lens[s]-q_len(s)+j come from
+ * window row q_start(s)+j instead (the speculative-verify side buffer, so that
+ * rejected drafts never touch the pool).
+ *
+ * This is the semantics of paged_attention_varlen / _materialised
+ * (memforge_ml/kernels/varlen_attention.py:78-235, 291-395) with every
+ * sequence's rows at consecutive positions, of paged_attention_blockwise
+ * (memforge_ml/kernels/block_attention.py:51-145) for one row, and of the
+ * Triton paged_decode_attention (memforge_ml/kernels/triton_paged_decode.py:
+ * 129-176) with q_per_seq = 1.  fp32 accumulation; the output has `dtype`.
+ * GQA: query head hq reads kv head hq / (num_q_heads / num_kv_heads).
+ * row_map (optional) sends logical row r to packed row row_map[r] for q, out
+ * and the window (arbitrary packing orders, varlen_attention.py:60-75).
+ */
+typedef struct {
+  uint32_t struct_size; /* sizeof(mf_attention_args) */
+  const void* q;        /* [rows][num_q_heads][head_dim] */
+  int64_t q_stride_row, q_stride_head;
+  void* out;            /* same indexing as q */
+  int64_t out_stride_row, out_stride_head;
+  const void* k_pool;   /* one layer of the pool */
+  const void* v_pool;
+  int64_t pool_stride_block, pool_stride_slot, pool_stride_head;
+  int32_t num_blocks, block_size;
+  const int32_t* block_tables; /* [num_seqs][table_stride] */
+  int32_t table_stride;
+  const int32_t* cu_seqlens_q; /* [num_seqs + 1] or NULL */
+  int32_t q_per_seq;           /* used when cu_seqlens_q is NULL */
+  const int32_t* kv_lens;      /* [num_seqs] */
+  const int32_t* row_map;      /* [total_q] or NULL */
+  const void* win_k;           /* [rows][num_kv_heads][head_dim] or NULL */
+  const void* win_v;
+  int64_t win_stride_row, win_stride_head;
+  int32_t num_seqs, total_q, max_q_len;
+  int32_t num_q_heads, num_kv_heads, head_dim;
+  float scale;
+  int32_t causal;
+  mf_dtype dtype;
+} mf_attention_args;
+
+/* Device workspace `mf_paged_attention` needs for these arguments on `device`
+ * (0 when none).  The caller allocates it once, ZERO-FILLED, and may reuse it
+ * for any later call with an equal or smaller requirement on the same stream:
+ * the kernels leave it zeroed.  Concurrent launches must not share one. */
+MF_API size_t mf_paged_attention_workspace_size(const mf_attention_args* args, int device);
+
+MF_API int mf_paged_attention(const mf_attention_args* args, void* workspace,
+                       size_t workspace_bytes, int32_t* err_flag, mf_stream_t stream);
+
+/*
+ * Triton-signature decode (memforge_ml/kernels/triton_paged_decode.py:129-176):
+ * q [B][Hq][D] (row stride q_stride_b, head stride q_stride_h), the layer's pool
+ * viewed flat [slots][Hkv][D] with strides (flat_stride_slot, flat_stride_head),
+ * block_tables int32 [B][table_stride], ctx_lens int32 [B] counting the new token,
+ * out [B][Hq][D] (contiguous).  A thin form of mf_paged_attention with
+ * q_per_seq = 1 over a pool of block_size-token blocks.
+ */
+MF_API int mf_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                    const void* key_flat, const void* value_flat,
+                    int64_t flat_stride_slot, int64_t flat_stride_head, int32_t num_slots,
+                    const int32_t* block_tables, int32_t table_stride,
+                    const int32_t* ctx_lens, int32_t batch, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                    float scale, mf_dtype dtype, void* out, void* workspace,
+                    size_t workspace_bytes, int32_t* err_flag, mf_stream_t stream);
+
+/*
+ * Copy-on-write block copy across all layers: for each pair i, block
+ * src[i] -> dst[i] in every layer of both pools (prefix_sharing.copy_block,
+ * memforge_ml/runtime/prefix_sharing.py:28-42).  Pools are contiguous
+ * [num_layers][num_blocks][block_elems] of `elem_bytes`-byte elements.
+ */
+MF_API int mf_copy_blocks(void* key_pool, void* value_pool, int32_t num_layers,
+                   int32_t num_blocks, int64_t block_elems, int32_t elem_bytes,
+                   const int32_t* src_dst_pairs, int32_t num_pairs, int32_t* err_flag,
+                   mf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEMFORGE_SM100_H */

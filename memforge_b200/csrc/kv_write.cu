@@ -1,0 +1,185 @@
+// KV writes into the paged pool: reshape_and_cache (slot-mapping scatter) and
+// the all-layer copy-on-write block copy.
+//
+// Both are byte-moving kernels bounded by HBM: every thread moves one 16-byte
+// vector (8 bf16 / 4 fp32 elements) when the row is 16-byte aligned, so each
+// warp issues fully coalesced 512-byte transactions along head_dim.
+
+#include "mf_internal.h"
+
+namespace mf {
+
+template <typename S, typename P>
+MF_DEVINL void copy_row_vec(const S* __restrict__ src, P* __restrict__ dst, int nvec_elems);
+
+template <typename S, typename P>
+__global__ void reshape_and_cache_kernel(const S* __restrict__ key, const S* __restrict__ value,
+                                         int64_t k_stride_tok, int64_t k_stride_head,
+                                         int64_t v_stride_tok, int64_t v_stride_head,
+                                         P* __restrict__ key_pool, P* __restrict__ value_pool,
+                                         int64_t sb, int64_t ss, int64_t sh, int64_t num_slots,
+                                         int32_t block_size, const void* __restrict__ slots,
+                                         int slots64, int num_tokens, int num_heads,
+                                         int head_dim, int vec, int32_t* err) {
+  // One work item = (token, head, vector of `vec` elements along head_dim).
+  const int vecs_per_row = head_dim / vec;
+  const int64_t total = (int64_t)num_tokens * num_heads * vecs_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vecs_per_row);
+    const int64_t th = i / vecs_per_row;
+    const int h = (int)(th % num_heads);
+    const int t = (int)(th / num_heads);
+    const int64_t slot = slots64 ? reinterpret_cast<const int64_t*>(slots)[t]
+                                 : (int64_t)reinterpret_cast<const int32_t*>(slots)[t];
+    if (slot < 0) {
+      if (slot != -1 && v == 0 && h == 0) set_err(err, MF_ERR_SLOT);
+      continue;
+    }
+    if (slot >= num_slots) {
+      if (v == 0 && h == 0) set_err(err, MF_ERR_SLOT);
+      continue;
+    }
+    const int64_t dst_off = (slot / block_size) * sb + (slot % block_size) * ss + h * sh + (int64_t)v * vec;
+    const S* ks = key + t * k_stride_tok + h * k_stride_head + (int64_t)v * vec;
+    const S* vs = value + t * v_stride_tok + h * v_stride_head + (int64_t)v * vec;
+    copy_row_vec<S, P>(ks, key_pool + dst_off, vec);
+    copy_row_vec<S, P>(vs, value_pool + dst_off, vec);
+  }
+}
+
+template <typename S, typename P>
+MF_DEVINL void copy_row_vec(const S* __restrict__ src, P* __restrict__ dst, int n) {
+  if constexpr (sizeof(S) == sizeof(P) && std::is_same<S, P>::value) {
+    if (n * sizeof(S) == 16) {
+      *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(src));
+    } else {
+      for (int j = 0; j < n; ++j) dst[j] = src[j];
+    }
+  } else {
+    // Widening is not supported; narrowing f32 -> f16/bf16 rounds like torch.
+    for (int j = 0; j < n; ++j) dst[j] = from_f32<P>(Elt<S>::to_f32(src[j]));
+  }
+}
+
+__global__ void copy_blocks_kernel(uint8_t* __restrict__ kp, uint8_t* __restrict__ vp,
+                                   int num_layers, int num_blocks, int64_t block_bytes,
+                                   const int32_t* __restrict__ pairs, int num_pairs,
+                                   int32_t* err) {
+  // grid.y = pair, grid.z = layer; threads stride the block's bytes in 16B units.
+  const int pair = blockIdx.y;
+  const int layer = blockIdx.z;
+  const int src = pairs[2 * pair];
+  const int dst = pairs[2 * pair + 1];
+  if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {
+    if (threadIdx.x == 0 && blockIdx.x == 0 && layer == 0) set_err(err, MF_ERR_BLOCK_ID);
+    return;
+  }
+  if (src == dst) return;
+  const int64_t layer_off = (int64_t)layer * num_blocks * block_bytes;
+  const int64_t n16 = block_bytes / 16;
+  const uint4* ks = reinterpret_cast<const uint4*>(kp + layer_off + (int64_t)src * block_bytes);
+  const uint4* vs = reinterpret_cast<const uint4*>(vp + layer_off + (int64_t)src * block_bytes);
+  uint4* kd = reinterpret_cast<uint4*>(kp + layer_off + (int64_t)dst * block_bytes);
+  uint4* vd = reinterpret_cast<uint4*>(vp + layer_off + (int64_t)dst * block_bytes);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    kd[i] = ks[i];
+    vd[i] = vs[i];
+  }
+}
+
+}  // namespace mf
+
+using namespace mf;
+
+namespace {
+
+template <typename S, typename P>
+int launch_rac(const void* key, const void* value, int64_t kst, int64_t ksh, int64_t vst,
+               int64_t vsh, void* kp, void* vp, int64_t sb, int64_t ss, int64_t sh,
+               int64_t num_slots, int32_t bs, const void* slots, int slots64, int T, int H,
+               int D, int32_t* err, cudaStream_t stream) {
+  // 16-byte vectors when every row start is 16-byte aligned, else scalar.
+  int vec = 1;
+  const int v16 = 16 / (int)sizeof(P);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (std::is_same<S, P>::value && D % v16 == 0 && al(key) && al(value) && al(kp) && al(vp) &&
+      (kst * sizeof(S)) % 16 == 0 && (ksh * sizeof(S)) % 16 == 0 &&
+      (vst * sizeof(S)) % 16 == 0 && (vsh * sizeof(S)) % 16 == 0 &&
+      (sb * sizeof(P)) % 16 == 0 && (ss * sizeof(P)) % 16 == 0 && (sh * sizeof(P)) % 16 == 0) {
+    vec = v16;
+  }
+  const int64_t items = (int64_t)T * H * (D / vec);
+  if (items == 0) return MF_OK;
+  const int threads = 256;
+  int64_t blocks = (items + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  reshape_and_cache_kernel<S, P><<<(unsigned)blocks, threads, 0, stream>>>(
+      static_cast<const S*>(key), static_cast<const S*>(value), kst, ksh, vst, vsh,
+      static_cast<P*>(kp), static_cast<P*>(vp), sb, ss, sh, num_slots, bs, slots, slots64, T, H,
+      D, vec, err);
+  return check_launch("reshape_and_cache");
+}
+
+}  // namespace
+
+extern "C" int mf_reshape_and_cache(const void* key, const void* value, mf_dtype src_dtype,
+                                    int64_t k_stride_tok, int64_t k_stride_head,
+                                    int64_t v_stride_tok, int64_t v_stride_head, void* key_pool,
+                                    void* value_pool, mf_dtype pool_dtype,
+                                    int64_t pool_stride_block, int64_t pool_stride_slot,
+                                    int64_t pool_stride_head, int32_t num_blocks,
+                                    int32_t block_size, const void* slot_mapping,
+                                    int32_t slot_mapping_is_int64, int32_t num_tokens,
+                                    int32_t num_kv_heads, int32_t head_dim, int32_t* err_flag,
+                                    mf_stream_t stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks <= 0)
+    return fail(MF_EINVAL, "reshape_and_cache: non-positive size");
+  if (num_tokens == 0) return MF_OK;
+  if (!key || !value || !key_pool || !value_pool || !slot_mapping)
+    return fail(MF_EINVAL, "reshape_and_cache: null pointer");
+  const int64_t num_slots = (int64_t)num_blocks * block_size;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+#define MF_RAC(S, P)                                                                          \
+  return launch_rac<S, P>(key, value, k_stride_tok, k_stride_head, v_stride_tok,              \
+                          v_stride_head, key_pool, value_pool, pool_stride_block,             \
+                          pool_stride_slot, pool_stride_head, num_slots, block_size,          \
+                          slot_mapping, slot_mapping_is_int64, num_tokens, num_kv_heads,      \
+                          head_dim, err_flag, s)
+  if (src_dtype == pool_dtype) {
+    if (pool_dtype == MF_F32) MF_RAC(float, float);
+    if (pool_dtype == MF_F16) MF_RAC(__half, __half);
+    if (pool_dtype == MF_BF16) MF_RAC(__nv_bfloat16, __nv_bfloat16);
+  } else if (src_dtype == MF_F32) {
+    if (pool_dtype == MF_F16) MF_RAC(float, __half);
+    if (pool_dtype == MF_BF16) MF_RAC(float, __nv_bfloat16);
+  }
+#undef MF_RAC
+  return fail(MF_EUNSUPPORTED, "reshape_and_cache: unsupported (src, pool) dtype pair");
+}
+
+extern "C" int mf_copy_blocks(void* key_pool, void* value_pool, int32_t num_layers,
+                              int32_t num_blocks, int64_t block_elems, int32_t elem_bytes,
+                              const int32_t* src_dst_pairs, int32_t num_pairs, int32_t* err_flag,
+                              mf_stream_t stream) {
+  if (num_pairs == 0) return MF_OK;
+  if (!key_pool || !value_pool || !src_dst_pairs || num_pairs < 0 || num_layers <= 0 ||
+      num_blocks <= 0 || block_elems <= 0 || elem_bytes <= 0)
+    return fail(MF_EINVAL, "copy_blocks: bad argument");
+  const int64_t block_bytes = block_elems * elem_bytes;
+  if (block_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(key_pool) & 15) ||
+      (reinterpret_cast<uintptr_t>(value_pool) & 15))
+    return fail(MF_EINVAL, "copy_blocks: blocks must be 16-byte multiples, pools 16-byte aligned");
+  if (num_pairs > 65535 || num_layers > 65535)
+    return fail(MF_EINVAL, "copy_blocks: at most 65535 pairs and layers per call");
+  const int64_t n16 = block_bytes / 16;
+  int gx = (int)((n16 + 255) / 256);
+  if (gx > 64) gx = 64;
+  dim3 grid(gx, num_pairs, num_layers);
+  copy_blocks_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), num_layers, num_blocks,
+      block_bytes, src_dst_pairs, num_pairs, err_flag);
+  return check_launch("copy_blocks");
+}

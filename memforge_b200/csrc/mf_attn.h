@@ -1,0 +1,63 @@
+// Parameters shared by the paged-attention kernels (device side view of
+// mf_attention_args plus derived values).
+#pragma once
+
+#include "mf_internal.h"
+
+namespace mf {
+
+struct AttnParams {
+  const void* q;
+  int64_t q_sr, q_sh;
+  void* out;
+  int64_t o_sr, o_sh;
+  const void* kp;
+  const void* vp;
+  int64_t sb, ss, sh;
+  int32_t num_blocks, block_size;
+  const int32_t* tables;
+  int32_t table_stride;
+  const int32_t* cu_q;
+  int32_t q_per_seq;
+  const int32_t* kv_lens;
+  const int32_t* row_map;
+  const void* wk;
+  const void* wv;
+  int64_t w_sr, w_sh;
+  int32_t num_seqs, total_q, max_q_len;
+  int32_t hq, hkv, d;
+  float scale;
+  int32_t causal;
+  int32_t* err;
+};
+
+// Query extent of sequence s.
+MF_DEVINL void seq_rows(const AttnParams& p, int s, int& q_start, int& q_len) {
+  if (p.cu_q) {
+    q_start = p.cu_q[s];
+    q_len = p.cu_q[s + 1] - q_start;
+  } else {
+    q_start = s * p.q_per_seq;
+    q_len = p.q_per_seq;
+  }
+}
+
+MF_DEVINL int map_row(const AttnParams& p, int r) { return p.row_map ? p.row_map[r] : r; }
+
+// Host launchers.
+int launch_attn_generic(const AttnParams& p, mf_dtype dtype, cudaStream_t stream);
+
+struct TcPlan {
+  bool ok = false;
+  const char* why = "";
+  int MT = 1, HG = 1, NHG = 1, PPS = 1, NS = 2, ctas = 0;
+  size_t smem = 0;
+  size_t part_floats = 0;   // floats per partial slot
+  size_t ws_bytes = 0;
+};
+
+TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool window);
+int launch_attn_tc(const AttnParams& p, mf_dtype dtype, const TcPlan& plan, void* ws,
+                   cudaStream_t stream);
+
+}  // namespace mf

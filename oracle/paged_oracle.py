@@ -48,7 +48,7 @@ def f32_to_bf16(x: np.ndarray) -> np.ndarray:
 
     This is the IEEE rounding torch applies in ``tensor.to(torch.bfloat16)``,
     which the reference's ``scatter_kv`` uses to cast into the pool dtype
-    (``paged_gather.py:113-114``).  NaN stays a quiet NaN.
+    (``paged_gather.py:113-114``).  Every NaN becomes torch's canonical 0x7FC0.
     """
     x = np.ascontiguousarray(x, dtype=np.float32)
     u = x.view(np.uint32).astype(np.uint64)
@@ -56,7 +56,7 @@ def f32_to_bf16(x: np.ndarray) -> np.ndarray:
     rounded = ((u + 0x7FFF + lsb) >> 16).astype(np.uint16)
     nan = np.isnan(x)
     if nan.any():
-        rounded = np.where(nan, ((u >> 16) | 0x40).astype(np.uint16), rounded)
+        rounded = np.where(nan, np.uint16(0x7FC0), rounded)
     return rounded.astype(np.uint16)
 
 
