@@ -9,19 +9,26 @@
 //    across ranges leaves fp32 partials (running max, sum, unnormalised
 //    accumulator) in the workspace and the last range to finish merges them
 //    with the log-sum-exp identity (a per-sequence arrival counter; no waiting).
-//  * One warp (the producer) walks the block table and issues one 4-D TMA
-//    tile load per page per K/V: box (64 dims, D/64, HG kv heads, 16 tokens)
-//    of the pool viewed as [slots][kv_heads][D], 128-byte swizzled, into a
-//    ring of shared-memory stages guarded by mbarriers.  No multicast.
-//  * Eight consumer warps each own one (kv head, 16-row m-tile): the rows are
-//    (query position, query head) pairs of the GQA group, so a page is read
-//    from HBM once for all query heads that share its kv head.  Scores and the
-//    PV product use mma.sync m16n8k16 with fp32 accumulation; the online
-//    softmax runs in registers in the log2 domain with quad shuffles.
-//  * When fewer than 8 (head, m-tile) pairs exist, the CTA runs PPS = 8/(HG*MT)
-//    independent virtual CTAs side by side, one page of each per stage.
+//  * One warp (the producer) walks the block tables and issues one 4-D TMA
+//    tile load per page per K/V: box (64 dims, 16 tokens, D/64, HG kv heads) of
+//    the pool viewed as [slots][kv_heads][D], 128-byte swizzled, into a ring
+//    of shared-memory stages guarded by mbarriers.  The box puts the 16 tokens
+//    of one (head, 64-dim half) in consecutive 128-byte rows, so the swizzle
+//    spreads every 8-token ldmatrix phase over all banks.  No multicast.
+//  * Eight consumer warps each own one (kv head, 16-row m-tile, half of D):
+//    rows are (query position, query head) pairs of the GQA group, so a page is
+//    read from HBM once for all query heads sharing its kv head.  Both halves
+//    compute the full Q K^T (mma.sync m16n8k16, fp32 accumulate); each keeps
+//    the P V accumulator for its half of head_dim, which keeps the streaming
+//    loop within the register budget of a 288-thread CTA.  Online softmax in
+//    the log2 domain with quad shuffles.
+//  * When fewer than 8 (head, m-tile, half) units exist, the CTA runs
+//    PPS = 8/units independent virtual CTAs side by side, one page each per stage.
 //  * Every mbarrier wait is bounded; on expiry the CTA sets MF_ERR_TIMEOUT,
 //    drains its own TMA loads and returns.
+//
+// Workspace: [0, SEM_REGION) arrival counters, always all-zero between launches
+// (each launch resets the ones it used); partial slots after it.
 
 #include "mf_attn.h"
 
@@ -32,44 +39,49 @@ namespace tc {
 constexpr int CONSUMER_WARPS = 8;
 constexpr int THREADS = (CONSUMER_WARPS + 1) * 32;
 constexpr int PAGE = 16;
+constexpr int DS = 2;  // consumer warps per (head, m-tile): halves of head_dim for P V
 constexpr uint64_t WAIT_LIMIT = 2000000000ull;  // 2 s of wall time per wait
 constexpr int MAX_SEQS = 4096;
+constexpr int MAX_WINDOW_SEQS = 1024;
+constexpr size_t SEM_REGION = size_t(1) << 20;
 
 struct Params {
   AttnParams a;
   int G, HG, NHG, MT, PPS, NS;
   int window;
   float scale_log2;
-  float* part;       // partial slots
-  int32_t* sems;     // arrival counters
-  int part_floats;   // floats per partial slot
+  float* part;      // partial slots
+  int32_t* sems;    // arrival counters
+  int part_floats;  // floats per partial slot
 };
 
 struct Smem {
-  // layout offsets (bytes from the 1024-aligned base)
-  uint32_t stage_bytes, page_bytes, bar_off, prefix_off, flag_off;
+  uint32_t page_bytes, stage_bytes, bar_off, prefix_off, qstart_off, flag_off, total;
 };
 
-__host__ __device__ inline Smem smem_layout(int D, int HG, int PPS, int NS, int B) {
+__host__ __device__ inline Smem smem_layout(int D, int HG, int PPS, int NS, int B, int window) {
   Smem s;
   s.page_bytes = (uint32_t)(HG * PAGE * D * 2);
   s.stage_bytes = 2u * PPS * s.page_bytes;
   s.bar_off = NS * s.stage_bytes;
   s.prefix_off = s.bar_off + 2 * NS * 8;
-  s.flag_off = s.prefix_off + (uint32_t)(B + 1) * 4;
+  s.qstart_off = s.prefix_off + (uint32_t)(B + 1) * 4;
+  s.flag_off = s.qstart_off + (window ? (uint32_t)B * 4 : 0u);
+  s.total = s.flag_off + 16;
   return s;
 }
 
-// Swizzled shared-memory address of the 16-byte chunk `chunk` (0..D/8-1) of
-// token `tok`, local kv head `hl`, in a page tile written by a 128B-swizzle TMA.
+// Swizzled shared-memory address of 16-byte chunk `chunk` (0..D/8-1) of token
+// `tok` of local kv head `hl` in a page tile written by the 128B-swizzle TMA
+// box (64, 16, D/64, HG): 128-byte row R = (hl * D/64 + chunk/8) * 16 + tok.
 template <int D>
-MF_DEVINL uint32_t tile_addr(uint32_t base, int tok, int hl, int chunk, int HG) {
+MF_DEVINL uint32_t tile_addr(uint32_t base, int tok, int hl, int chunk) {
   const int half = chunk >> 3, cc = chunk & 7;
-  const int R = (tok * HG + hl) * (D / 64) + half;
+  const int R = ((hl * (D / 64) + half) << 4) + tok;
   return base + (uint32_t)(R * 128) + (uint32_t)((cc ^ (R & 7)) << 4);
 }
 
-// Page geometry of sequence i (identical in producer and consumers).
+// Page geometry of sequence i (identical in the prologue and the consumers).
 struct SeqGeo {
   int q_start, q_len, kv_len, pool_len, pool_pages, pages;
 };
@@ -93,7 +105,7 @@ MF_DEVINL SeqGeo seq_geo(const Params& P, int i) {
   return g;
 }
 
-// Virtual-CTA boundaries: range of vc is [bound(vc), bound(vc+1)).
+// Virtual-CTA boundaries: the range of vc is [bound(vc), bound(vc+1)).
 MF_DEVINL int64_t bound(int64_t vc, int64_t total, int64_t NV) { return vc * total / NV; }
 
 MF_DEVINL int owner(int64_t page, int64_t total, int64_t NV) {
@@ -113,6 +125,36 @@ MF_DEVINL int find_seq(const int* prefix, int B, int off) {
   return lo;
 }
 
+// Position in the virtual page list, advanced one page at a time from shared
+// memory only (no global loads).
+struct Cursor {
+  int hg, i, k, pages;
+};
+
+MF_DEVINL Cursor cursor_at(const int* prefix, int B, int64_t T1, int64_t v) {
+  Cursor c;
+  c.hg = (int)(v / T1);
+  const int off = (int)(v - (int64_t)c.hg * T1);
+  c.i = find_seq(prefix, B, off);
+  c.k = off - prefix[c.i];
+  c.pages = prefix[c.i + 1] - prefix[c.i];
+  return c;
+}
+
+// Only called while the next page is inside the range, so a non-empty
+// sequence always follows.
+MF_DEVINL void cursor_next(Cursor& c, const int* prefix, int B) {
+  if (++c.k < c.pages) return;
+  c.k = 0;
+  do {
+    if (++c.i == B) {
+      c.i = 0;
+      ++c.hg;
+    }
+    c.pages = prefix[c.i + 1] - prefix[c.i];
+  } while (c.pages == 0);
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -123,14 +165,15 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw_base);
   const int B = P.a.num_seqs;
-  const Smem L = smem_layout(D, P.HG, P.PPS, P.NS, B);
+  const Smem L = smem_layout(D, P.HG, P.PPS, P.NS, B, P.window);
   uint64_t* full = reinterpret_cast<uint64_t*>(gbase + L.bar_off);
   uint64_t* empty = full + P.NS;
   int* prefix = reinterpret_cast<int*>(gbase + L.prefix_off);
+  int* qstart = reinterpret_cast<int*>(gbase + L.qstart_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L.flag_off);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int units = P.HG * P.MT;           // (head, m-tile) pairs per page
+  const int units = P.HG * P.MT * DS;      // consumer units per page
   const int active_warps = units * P.PPS;  // consumer warps with work
 
   // ---------------------------------------------------------------- prologue
@@ -144,14 +187,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   }
   for (int i = tid; i < B; i += blockDim.x) {
     const SeqGeo g = seq_geo(P, i);
-    int q_start, q_len;
-    seq_rows(P.a, i, q_start, q_len);
-    if (q_len > 0 && g.pages == 0) set_err(P.a.err, MF_ERR_LENGTH);
-    if (g.pages > 0) {
-      const int need = (g.pool_len + PAGE - 1) / PAGE;
-      if (need > P.a.table_stride) set_err(P.a.err, MF_ERR_TABLE);
-    }
+    if (g.q_len > 0 && g.pages == 0) set_err(P.a.err, MF_ERR_LENGTH);
+    if (g.pages > 0 && (g.pool_len + PAGE - 1) / PAGE > P.a.table_stride)
+      set_err(P.a.err, MF_ERR_TABLE);
     prefix[i + 1] = g.pages;
+    if (P.window) qstart[i] = g.q_start;
   }
   __syncthreads();
   if (warp == 0) {
@@ -178,8 +218,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   // Longest virtual-CTA range of this CTA: every consumer loops this many stages.
   int max_len = 0;
   for (int j = 0; j < P.PPS; ++j) {
-    const int64_t vc = (int64_t)blockIdx.x * P.PPS + j;
-    max_len = max(max_len, (int)(bound(vc + 1, TP, NV) - bound(vc, TP, NV)));
+    const int64_t vcj = (int64_t)blockIdx.x * P.PPS + j;
+    max_len = max(max_len, (int)(bound(vcj + 1, TP, NV) - bound(vcj, TP, NV)));
   }
   if (max_len == 0) return;
 
@@ -189,33 +229,32 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
     if (lane == 0) {
       prefetch_tmap(&tmk);
       prefetch_tmap(&tmv);
-      if (P.window) { prefetch_tmap(&twk); prefetch_tmap(&twv); }
+      if (P.window) {
+        prefetch_tmap(&twk);
+        prefetch_tmap(&twv);
+      }
     }
-    // Lane j < PPS feeds virtual CTA j; block ids are fetched two pages ahead.
+    // Lane j < PPS feeds virtual CTA j; block ids are loaded two pages ahead.
     const bool feeder = lane < P.PPS;
     const int64_t vc = (int64_t)blockIdx.x * P.PPS + lane;
     const int64_t lo = feeder ? bound(vc, TP, NV) : 0;
     const int len = feeder ? (int)(bound(vc + 1, TP, NV) - lo) : 0;
-    auto page_src = [&](int it, int& hg, int& i, int& k, int& is_win) {
-      const int64_t v = lo + it;
-      hg = (int)(v / T1);
-      const int off = (int)(v - (int64_t)hg * T1);
-      i = find_seq(prefix, B, off);
-      k = off - prefix[i];
-      const SeqGeo g = seq_geo(P, i);
-      is_win = (P.window && k == g.pool_pages) ? 1 : 0;
-      return g;
+    auto block_of = [&](const Cursor& c) -> int {
+      if (P.window && c.k == c.pages - 1) return 0;  // window page: no table entry
+      return __ldg(P.a.tables + (int64_t)c.i * P.a.table_stride + c.k);
     };
-    auto fetch_block = [&](int it) -> int {
-      if (!feeder || it >= len) return 0;
-      int hg, i, k, w;
-      page_src(it, hg, i, k, w);
-      if (w) return 0;
-      return __ldg(P.a.tables + (int64_t)i * P.a.table_stride + k);
-    };
-    int blk0 = fetch_block(0), blk1 = fetch_block(1);
+    Cursor cur{0, 0, 0, 1}, ahead{0, 0, 0, 1};
+    int blk0 = 0, blk1 = 0;
+    if (len > 0) {
+      cur = cursor_at(prefix, B, T1, lo);
+      ahead = cur;
+      blk0 = block_of(cur);
+      if (len > 1) {
+        cursor_next(ahead, prefix, B);
+        blk1 = block_of(ahead);
+      }
+    }
     int armed = 0;
-    bool ok = true;
     for (int it = 0; it < max_len; ++it) {
       const int stage = it % P.NS;
       if (it >= P.NS) {
@@ -224,11 +263,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
           *abort_flag = 1;
         }
         __syncwarp();
-        if (*abort_flag) { ok = false; break; }
+        if (*abort_flag) break;
       }
-      const int blk2 = fetch_block(it + 2);
-      // Pages this stage carries.
-      int n = 0;
+      int n = 0;  // pages this stage carries
       for (int j = 0; j < P.PPS; ++j) {
         const int64_t vcj = (int64_t)blockIdx.x * P.PPS + j;
         if (it < (int)(bound(vcj + 1, TP, NV) - bound(vcj, TP, NV))) ++n;
@@ -236,32 +273,35 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
       if (lane == 0) mbar_arrive_expect_tx(&full[stage], (uint32_t)n * 2u * L.page_bytes);
       __syncwarp();
       if (feeder && it < len) {
-        int hg, i, k, w;
-        const SeqGeo g = page_src(it, hg, i, k, w);
         uint8_t* sk = gbase + stage * L.stage_bytes + lane * L.page_bytes;
         uint8_t* sv = sk + P.PPS * L.page_bytes;
-        if (w) {
-          tma_load_4d(sk, &twk, &full[stage], 0, 0, hg * P.HG, map_row(P.a, g.q_start), pol);
-          tma_load_4d(sv, &twv, &full[stage], 0, 0, hg * P.HG, map_row(P.a, g.q_start), pol);
+        if (P.window && cur.k == cur.pages - 1) {
+          const int row = qstart[cur.i];
+          tma_load_4d(sk, &twk, &full[stage], 0, row, 0, cur.hg * P.HG, pol);
+          tma_load_4d(sv, &twv, &full[stage], 0, row, 0, cur.hg * P.HG, pol);
         } else {
           int blk = blk0;
           if (blk < 0 || blk >= P.a.num_blocks) {
             set_err(P.a.err, MF_ERR_BLOCK_ID);
             blk = 0;
           }
-          tma_load_4d(sk, &tmk, &full[stage], 0, 0, hg * P.HG, blk * PAGE, pol);
-          tma_load_4d(sv, &tmv, &full[stage], 0, 0, hg * P.HG, blk * PAGE, pol);
+          tma_load_4d(sk, &tmk, &full[stage], 0, blk * PAGE, 0, cur.hg * P.HG, pol);
+          tma_load_4d(sv, &tmv, &full[stage], 0, blk * PAGE, 0, cur.hg * P.HG, pol);
         }
+        int blk2 = 0;
+        if (it + 2 < len) {
+          cursor_next(ahead, prefix, B);
+          blk2 = block_of(ahead);
+        }
+        if (it + 1 < len) cursor_next(cur, prefix, B);
+        blk0 = blk1;
+        blk1 = blk2;
       }
-      blk0 = blk1;
-      blk1 = blk2;
       armed = it + 1;
     }
-    (void)ok;
     // Drain: no TMA write may still target this CTA's shared memory at exit.
     if (lane == 0) {
-      const int first = max(0, armed - P.NS);
-      for (int it = first; it < armed; ++it) {
+      for (int it = max(0, armed - P.NS); it < armed; ++it) {
         if (!mbar_wait_bounded(&full[it % P.NS], (it / P.NS) & 1, WAIT_LIMIT))
           set_err(P.a.err, MF_ERR_TIMEOUT);
       }
@@ -272,10 +312,13 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   // ============================================================== consumers
   if (warp >= active_warps) return;
   using M = Mma<T>;
-  const int pair = warp % units;
+  constexpr int DH = D / 2;          // head_dim columns this warp accumulates
+  const int u = warp % units;
   const int ps = warp / units;       // virtual CTA within this CTA
-  const int hl = pair / P.MT;        // local kv head
+  const int dh = u % DS;             // which half of head_dim
+  const int pair = u / DS;
   const int mt = pair % P.MT;        // m-tile
+  const int hl = pair / P.MT;        // local kv head
   const int g4 = lane >> 2, c4 = lane & 3;
   const int64_t vc = (int64_t)blockIdx.x * P.PPS + ps;
   const int64_t lo = bound(vc, TP, NV);
@@ -284,60 +327,154 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   T* obase = static_cast<T*>(P.a.out);
   const float sl2 = P.scale_log2;
 
-  // Piece state.
   int hg = 0, si = 0, k = 0, k0 = 0;
   SeqGeo geo{};
   bool first_piece = true;
+  int n_merge = 0, merge_hg0 = 0, merge_si0 = 0, merge_hg1 = 0, merge_si1 = 0;
   uint32_t qf[D / 16][4];
-  float o[D / 8][4];
+  float o[DH / 8][4];
   float mrow[2], lrow[2];
 
-  auto start_piece = [&](int64_t v) {
-    hg = (int)(v / T1);
-    const int off = (int)(v - (int64_t)hg * T1);
-    si = find_seq(prefix, B, off);
-    k = off - prefix[si];
-    k0 = k;
-    geo = seq_geo(P, si);
-    const int head = hg * P.HG + hl;
+  for (int it = 0; it < max_len; ++it) {
+    const int stage = it % P.NS;
+    if (it >= len) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      continue;
+    }
+    if (it == 0 || k == geo.pages) {
+      // ---------------------------------------------------- start a piece
+      const Cursor c = cursor_at(prefix, B, T1, lo + it);
+      hg = c.hg;
+      si = c.i;
+      k = c.k;
+      k0 = k;
+      geo = seq_geo(P, si);
+      const int head = hg * P.HG + hl;
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      const int r = mt * 16 + g4 + 8 * h2;
-      const int qi = r / P.G, gg = r % P.G;
-      const bool valid = qi < geo.q_len;
-      const T* qrow = valid ? qbase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.q_sr +
-                                  (int64_t)(head * P.G + gg) * P.a.q_sh
-                            : nullptr;
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int r = mt * 16 + g4 + 8 * h2;
+        const int qi = r / P.G, gg = r % P.G;
+        const bool valid = qi < geo.q_len;
+        const T* qrow = qbase + (valid ? (int64_t)map_row(P.a, geo.q_start + qi) * P.a.q_sr +
+                                             (int64_t)(head * P.G + gg) * P.a.q_sh
+                                       : 0);
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        uint32_t lo32 = 0, hi32 = 0;
-        if (valid) {
-          lo32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c4);
-          hi32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c4);
+        for (int ks = 0; ks < D / 16; ++ks) {
+          uint32_t lo32 = 0, hi32 = 0;
+          if (valid) {
+            lo32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c4);
+            hi32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c4);
+          }
+          qf[ks][h2] = lo32;      // rows g / g+8, k 0..7 of the step
+          qf[ks][2 + h2] = hi32;  // rows g / g+8, k 8..15
         }
-        qf[ks][h2] = lo32;       // a0a1 (row g) / a2a3 (row g+8)
-        qf[ks][2 + h2] = hi32;   // a4a5 / a6a7
+      }
+#pragma unroll
+      for (int n = 0; n < DH / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      mrow[0] = mrow[1] = -INFINITY;
+      lrow[0] = lrow[1] = 0.f;
+    }
+
+    if (!mbar_wait_bounded(&full[stage], (it / P.NS) & 1, WAIT_LIMIT)) {
+      if (lane == 0) set_err(P.a.err, MF_ERR_TIMEOUT);
+      *abort_flag = 1;
+    }
+    if (__any_sync(0xffffffffu, *abort_flag != 0)) return;
+
+    const uint32_t sK = base + stage * L.stage_bytes + ps * L.page_bytes;
+    const uint32_t sV = sK + P.PPS * L.page_bytes;
+    const bool is_win = P.window && k == geo.pool_pages;
+    const int kbase = is_win ? geo.pool_len : k * PAGE;
+    const int valid = is_win ? geo.q_len : min(PAGE, geo.pool_len - k * PAGE);
+    const int win_start = geo.kv_len - geo.q_len;
+    const bool need_mask = valid < PAGE || (P.a.causal && kbase + PAGE - 1 > win_start);
+
+    // S = Q K^T for 16 rows x 16 tokens (full head_dim)
+    float sc[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      const int tok = (lane & 7) + ((lane >> 4) << 3);
+      const int chunk = ks * 2 + ((lane >> 3) & 1);
+      ldsm_x4(b0, b1, b2, b3, tile_addr<D>(sK, tok, hl, chunk));
+      M::run(sc[0], qf[ks], b0, b1);
+      M::run(sc[1], qf[ks], b2, b3);
+    }
+    // online softmax (log2 domain)
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float s = sc[n][e] * sl2;
+        if (need_mask) {
+          const int tok = n * 8 + 2 * c4 + (e & 1);
+          const int r = mt * 16 + g4 + 8 * (e >> 1);
+          const int lim = P.a.causal ? win_start + r / P.G : geo.kv_len - 1;
+          if (tok >= valid || kbase + tok > lim) s = -INFINITY;
+        }
+        sc[n][e] = s;
+        mx[e >> 1] = fmaxf(mx[e >> 1], s);
       }
     }
+    uint32_t pa[4];
 #pragma unroll
-    for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    mrow[0] = mrow[1] = -INFINITY;
-    lrow[0] = lrow[1] = 0.f;
-  };
+    for (int h2 = 0; h2 < 2; ++h2) {
+      mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 1));
+      mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 2));
+      const float mnew = fmaxf(mrow[h2], mx[h2]);
+      const float mu = (mnew == -INFINITY) ? 0.f : mnew;
+      const float alpha = fast_exp2(mrow[h2] - mu);
+      mrow[h2] = mnew;
+      const float p0 = fast_exp2(sc[0][2 * h2] - mu), p1 = fast_exp2(sc[0][2 * h2 + 1] - mu);
+      const float p2 = fast_exp2(sc[1][2 * h2] - mu), p3 = fast_exp2(sc[1][2 * h2 + 1] - mu);
+      lrow[h2] = lrow[h2] * alpha + (p0 + p1 + p2 + p3);
+#pragma unroll
+      for (int n = 0; n < DH / 8; ++n) {
+        o[n][2 * h2] *= alpha;
+        o[n][2 * h2 + 1] *= alpha;
+      }
+      pa[h2] = M::pack(p0, p1);      // rows g / g+8, tokens 2c..2c+1
+      pa[2 + h2] = M::pack(p2, p3);  // rows g / g+8, tokens 8+2c..
+    }
+    // O[:, dh half] += P V
+#pragma unroll
+    for (int np = 0; np < DH / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      const int tok = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int chunk = dh * (DH / 8) + np * 2 + (lane >> 4);
+      ldsm_x4_trans(b0, b1, b2, b3, tile_addr<D>(sV, tok, hl, chunk));
+      if (valid < PAGE) {
+        // Unwritten slots may hold anything (NaN included): zero them so that
+        // p = 0 really contributes nothing.
+        const int t_lo = 2 * c4, t_hi = 8 + 2 * c4;
+        const uint32_t mlo = (t_lo < valid ? 0xffffu : 0u) | (t_lo + 1 < valid ? 0xffff0000u : 0u);
+        const uint32_t mhi = (t_hi < valid ? 0xffffu : 0u) | (t_hi + 1 < valid ? 0xffff0000u : 0u);
+        b0 &= mlo;
+        b1 &= mhi;
+        b2 &= mlo;
+        b3 &= mhi;
+      }
+      M::run(o[2 * np], pa, b0, b1);
+      M::run(o[2 * np + 1], pa, b2, b3);
+    }
+    ++k;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
 
-  auto finish_piece = [&]() {
-    // quad-reduce the per-thread partial row sums
+    if (k != geo.pages && it != len - 1) continue;
+    // ------------------------------------------------------ finish a piece
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
       lrow[h2] += __shfl_xor_sync(0xffffffffu, lrow[h2], 1);
       lrow[h2] += __shfl_xor_sync(0xffffffffu, lrow[h2], 2);
     }
     const int head = hg * P.HG + hl;
-    const bool whole = (k0 == 0 && k == geo.pages);
-    const int64_t vs = (int64_t)hg * B + si;
-    const int64_t vstart = (int64_t)hg * T1 + prefix[si];
-    const int64_t vend = vstart + geo.pages;
-    if (whole) {
+    if (k0 == 0 && k == geo.pages) {
+      // The piece is the whole sequence: write the output rows directly.
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const int r = mt * 16 + g4 + 8 * h2;
@@ -345,189 +482,111 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
         if (qi >= geo.q_len) continue;
         const float inv = lrow[h2] > 0.f ? 1.f / lrow[h2] : 0.f;
         T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
-                  (int64_t)(head * P.G + gg) * P.a.o_sh;
+                  (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
 #pragma unroll
-        for (int n = 0; n < D / 8; ++n) {
+        for (int n = 0; n < DH / 8; ++n) {
           *reinterpret_cast<uint32_t*>(orow + n * 8 + 2 * c4) =
               M::pack(o[n][2 * h2] * inv, o[n][2 * h2 + 1] * inv);
         }
       }
       first_piece = false;
-      return;
+      continue;
     }
     // Partial: slot 0 when this piece starts the virtual CTA's range.
     const int slot = first_piece ? 0 : 1;
     first_piece = false;
-    float* part = P.part + ((vc * 2 + slot) * (int64_t)P.part_floats);
-    const int rows_total = P.HG * P.MT * 16;
-    float* pacc = part + (int64_t)((hl * P.MT + mt) * 16) * D;
-    float* pm = part + (int64_t)rows_total * D + (hl * P.MT + mt) * 16;
-    float* pl = pm + rows_total;
+    const int unit = (hl * P.MT + mt) * DS + dh;
+    const int unit_rows = P.HG * P.MT * DS * 16;
+    {
+      float* part = P.part + (vc * 2 + slot) * (int64_t)P.part_floats;
+      float* pacc = part + (int64_t)(unit * 16) * DH;
+      float* pm = part + (int64_t)unit_rows * DH + unit * 16;
 #pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      const int rr = g4 + 8 * h2;
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int rr = g4 + 8 * h2;
 #pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        *reinterpret_cast<float2*>(pacc + rr * D + n * 8 + 2 * c4) =
-            make_float2(o[n][2 * h2], o[n][2 * h2 + 1]);
-      }
-      if (c4 == 0) {
-        pm[rr] = mrow[h2];
-        pl[rr] = lrow[h2];
+        for (int n = 0; n < DH / 8; ++n)
+          *reinterpret_cast<float2*>(pacc + rr * DH + n * 8 + 2 * c4) =
+              make_float2(o[n][2 * h2], o[n][2 * h2 + 1]);
+        if (c4 == 0) {
+          pm[rr] = mrow[h2];
+          pm[unit_rows + rr] = lrow[h2];
+        }
       }
     }
     __threadfence();
     __syncwarp();
-    int32_t* sem = P.sems + (vs * P.HG + hl) * P.MT + mt;
+    const int64_t vstart = (int64_t)hg * T1 + prefix[si];
+    const int64_t vend = vstart + geo.pages;
     const int vc0 = owner(vstart, TP, NV);
     const int vc1 = owner(vend - 1, TP, NV);
+    // Ranges covering this sequence: [vc0, vc1] minus empty ones (a virtual CTA
+    // owns no page when there are fewer pages than ranges).
+    int covering = 0;
+    for (int c = vc0; c <= vc1; ++c) covering += bound(c + 1, TP, NV) > bound(c, TP, NV);
+    int32_t* sem = P.sems + (((int64_t)hg * B + si) * P.HG + hl) * (P.MT * DS) + mt * DS + dh;
     int old = 0;
     if (lane == 0) old = atomicAdd(sem, 1);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != vc1 - vc0) return;
-    // Last arrival for this (sequence, head, m-tile): merge every range's partial.
+    if (old != covering - 1) continue;
+    // Last arrival for this (sequence, head, m-tile, half): merge after the
+    // streaming loop (at most two per virtual CTA: its first and last piece).
+    if (n_merge == 0) {
+      merge_hg0 = hg;
+      merge_si0 = si;
+    } else {
+      merge_hg1 = hg;
+      merge_si1 = si;
+    }
+    ++n_merge;
+  }
+
+  for (int m = 0; m < n_merge; ++m) {
+    const int mhg = m == 0 ? merge_hg0 : merge_hg1;
+    const int msi = m == 0 ? merge_si0 : merge_si1;
+    const SeqGeo mg = seq_geo(P, msi);
+    const int head = mhg * P.HG + hl;
+    const int unit = (hl * P.MT + mt) * DS + dh;
+    const int unit_rows = P.HG * P.MT * DS * 16;
+    const int64_t vstart = (int64_t)mhg * T1 + prefix[msi];
+    const int vc0 = owner(vstart, TP, NV);
+    const int vc1 = owner(vstart + mg.pages - 1, TP, NV);
+    int32_t* sem = P.sems + (((int64_t)mhg * B + msi) * P.HG + hl) * (P.MT * DS) + mt * DS + dh;
     __threadfence();
     for (int rr = 0; rr < 16; ++rr) {
       const int r = mt * 16 + rr;
       const int qi = r / P.G, gg = r % P.G;
-      if (qi >= geo.q_len) continue;
+      if (qi >= mg.q_len) continue;
       float Mx = -INFINITY;
       for (int c = vc0; c <= vc1; ++c) {
+        if (bound(c + 1, TP, NV) == bound(c, TP, NV)) continue;  // empty range
         const int sl = (bound(c, TP, NV) >= vstart) ? 0 : 1;
-        const float* pp = P.part + (int64_t)(c * 2 + sl) * P.part_floats +
-                          (int64_t)rows_total * D + (hl * P.MT + mt) * 16;
-        Mx = fmaxf(Mx, __ldcg(pp + rr));
+        const float* pp = P.part + (int64_t)(c * 2 + sl) * P.part_floats;
+        Mx = fmaxf(Mx, __ldcg(pp + (int64_t)unit_rows * DH + unit * 16 + rr));
       }
       const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
       float Ls = 0.f;
-      float acc[D / 32];
+      float acc[DH / 32];
 #pragma unroll
-      for (int e = 0; e < D / 32; ++e) acc[e] = 0.f;
+      for (int e = 0; e < DH / 32; ++e) acc[e] = 0.f;
       for (int c = vc0; c <= vc1; ++c) {
+        if (bound(c + 1, TP, NV) == bound(c, TP, NV)) continue;
         const int sl = (bound(c, TP, NV) >= vstart) ? 0 : 1;
         const float* pp = P.part + (int64_t)(c * 2 + sl) * P.part_floats;
-        const float* ppm = pp + (int64_t)rows_total * D + (hl * P.MT + mt) * 16;
-        const float mk = __ldcg(ppm + rr);
+        const float mk = __ldcg(pp + (int64_t)unit_rows * DH + unit * 16 + rr);
         const float w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - Mu);
-        Ls += w * __ldcg(ppm + rows_total + rr);
-        const float* pa = pp + (int64_t)((hl * P.MT + mt) * 16 + rr) * D;
+        Ls += w * __ldcg(pp + (int64_t)unit_rows * DH + unit_rows + unit * 16 + rr);
+        const float* pa2 = pp + (int64_t)(unit * 16 + rr) * DH;
 #pragma unroll
-        for (int e = 0; e < D / 32; ++e) acc[e] += w * __ldcg(pa + lane + 32 * e);
+        for (int e = 0; e < DH / 32; ++e) acc[e] += w * __ldcg(pa2 + lane + 32 * e);
       }
       const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-      T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
-                (int64_t)(head * P.G + gg) * P.a.o_sh;
+      T* orow = obase + (int64_t)map_row(P.a, mg.q_start + qi) * P.a.o_sr +
+                (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
 #pragma unroll
-      for (int e = 0; e < D / 32; ++e) orow[lane + 32 * e] = from_f32<T>(acc[e] * inv);
+      for (int e = 0; e < DH / 32; ++e) orow[lane + 32 * e] = from_f32<T>(acc[e] * inv);
     }
     if (lane == 0) *sem = 0;  // leave the counter zeroed for the next launch
-  };
-
-  bool have_piece = false;
-  for (int it = 0; it < max_len; ++it) {
-    const int stage = it % P.NS;
-    if (it < len) {
-      if (!have_piece) {
-        start_piece(lo + it);
-        have_piece = true;
-      }
-      bool ok = true;
-      if (!mbar_wait_bounded(&full[stage], (it / P.NS) & 1, WAIT_LIMIT)) {
-        if (lane == 0) set_err(P.a.err, MF_ERR_TIMEOUT);
-        ok = false;
-      }
-      if (!__all_sync(0xffffffffu, ok) || *abort_flag) {
-        *abort_flag = 1;
-        return;
-      }
-      const uint32_t sK = base + stage * L.stage_bytes + ps * L.page_bytes;
-      const uint32_t sV = sK + P.PPS * L.page_bytes;
-      const bool is_win = P.window && k == geo.pool_pages;
-      const int kbase = is_win ? geo.pool_len : k * PAGE;
-      const int valid = is_win ? geo.q_len : min(PAGE, geo.pool_len - k * PAGE);
-      const int win_start = geo.kv_len - geo.q_len;
-      const bool need_mask = valid < PAGE || (P.a.causal && kbase + PAGE - 1 > win_start);
-
-      // S = Q K^T for 16 rows x 16 tokens
-      float sc[2][4];
-#pragma unroll
-      for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        uint32_t b0, b1, b2, b3;
-        const int tok = (lane & 7) + ((lane >> 4) << 3);
-        const int chunk = ks * 2 + ((lane >> 3) & 1);
-        ldsm_x4(b0, b1, b2, b3, tile_addr<D>(sK, tok, hl, chunk, P.HG));
-        M::run(sc[0], qf[ks], b0, b1);
-        M::run(sc[1], qf[ks], b2, b3);
-      }
-      // online softmax (log2 domain)
-      float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-      for (int n = 0; n < 2; ++n) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float s = sc[n][e] * sl2;
-          if (need_mask) {
-            const int tok = n * 8 + 2 * c4 + (e & 1);
-            const int r = mt * 16 + g4 + 8 * (e >> 1);
-            const int lim = P.a.causal ? win_start + r / P.G : geo.kv_len - 1;
-            if (tok >= valid || kbase + tok > lim) s = -INFINITY;
-          }
-          sc[n][e] = s;
-          mx[e >> 1] = fmaxf(mx[e >> 1], s);
-        }
-      }
-      uint32_t pa[4];
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 1));
-        mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 2));
-        const float mnew = fmaxf(mrow[h2], mx[h2]);
-        const float mu = (mnew == -INFINITY) ? 0.f : mnew;
-        const float alpha = fast_exp2(mrow[h2] - mu);
-        mrow[h2] = mnew;
-        const float p0 = fast_exp2(sc[0][2 * h2] - mu), p1 = fast_exp2(sc[0][2 * h2 + 1] - mu);
-        const float p2 = fast_exp2(sc[1][2 * h2] - mu), p3 = fast_exp2(sc[1][2 * h2 + 1] - mu);
-        lrow[h2] = lrow[h2] * alpha + (p0 + p1 + p2 + p3);
-#pragma unroll
-        for (int n = 0; n < D / 8; ++n) {
-          o[n][2 * h2] *= alpha;
-          o[n][2 * h2 + 1] *= alpha;
-        }
-        pa[h2] = M::pack(p0, p1);      // (row g / g+8, tokens 2c..2c+1)
-        pa[2 + h2] = M::pack(p2, p3);  // (row g / g+8, tokens 8+2c..)
-      }
-      // O += P V
-#pragma unroll
-      for (int np = 0; np < D / 16; ++np) {
-        uint32_t b0, b1, b2, b3;
-        const int tok = (lane & 7) + (((lane >> 3) & 1) << 3);
-        const int chunk = np * 2 + (lane >> 4);
-        ldsm_x4_trans(b0, b1, b2, b3, tile_addr<D>(sV, tok, hl, chunk, P.HG));
-        if (valid < PAGE) {
-          // Unwritten slots may hold anything (NaN included): zero them so
-          // that p = 0 really contributes nothing.
-          const int t_lo = 2 * c4, t_hi = 8 + 2 * c4;
-          const uint32_t mlo = (t_lo < valid ? 0xffffu : 0u) | (t_lo + 1 < valid ? 0xffff0000u : 0u);
-          const uint32_t mhi = (t_hi < valid ? 0xffffu : 0u) | (t_hi + 1 < valid ? 0xffff0000u : 0u);
-          b0 &= mlo; b1 &= mhi; b2 &= mlo; b3 &= mhi;
-        }
-        M::run(o[2 * np], pa, b0, b1);
-        M::run(o[2 * np + 1], pa, b2, b3);
-      }
-      ++k;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      // A piece ends with its sequence or with this virtual CTA's range.
-      if (k == geo.pages || it == len - 1) {
-        finish_piece();
-        have_piece = false;
-      }
-    } else {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-    }
   }
 }
 
@@ -535,7 +594,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
 
 TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool window) {
   TcPlan pl;
-  auto no = [&](const char* why) { pl.ok = false; pl.why = why; return pl; };
+  auto no = [&](const char* why) {
+    pl.ok = false;
+    pl.why = why;
+    return pl;
+  };
   if (dtype != MF_BF16 && dtype != MF_F16) return no("dtype is not bf16/f16");
   if (p.d != 64 && p.d != 128) return no("head_dim is not 64 or 128");
   if (p.block_size != tc::PAGE) return no("block_size is not 16");
@@ -553,33 +616,40 @@ TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool wind
   if (rows > 64 || rows <= 0) return no("more than 64 rows per kv head");
   if (window) {
     if (p.max_q_len > tc::PAGE) return no("window longer than one page");
+    if (p.num_seqs > tc::MAX_WINDOW_SEQS) return no("window batch above 1024 sequences");
     if ((p.w_sr * 2) % 16 || (p.w_sh * 2) % 16) return no("window strides not 16-byte multiples");
     if ((reinterpret_cast<uintptr_t>(p.wk) | reinterpret_cast<uintptr_t>(p.wv)) & 15)
       return no("window base not 16-byte aligned");
     if (p.row_map) return no("window with row_map");
   }
   pl.MT = (rows + 15) / 16;
-  const int cap = 8 / pl.MT;
+  const int per_head = pl.MT * tc::DS;
+  const int cap = tc::CONSUMER_WARPS / per_head;
   pl.HG = 1;
   for (int hg = cap; hg >= 1; --hg)
-    if (p.hkv % hg == 0) { pl.HG = hg; break; }
+    if (p.hkv % hg == 0) {
+      pl.HG = hg;
+      break;
+    }
   pl.NHG = p.hkv / pl.HG;
-  pl.PPS = 8 / (pl.HG * pl.MT);
+  pl.PPS = tc::CONSUMER_WARPS / (pl.HG * per_head);
   if (pl.PPS < 1) pl.PPS = 1;
+  const size_t sem_bytes = (size_t)p.num_seqs * p.hkv * per_head * sizeof(int32_t);
+  if (sem_bytes > tc::SEM_REGION) return no("too many (sequence, head) counters");
   const int budget = 227 * 1024 - 1024;  // opt-in maximum minus alignment slack
-  auto layout = [&](int ns) { return tc::smem_layout(p.d, pl.HG, pl.PPS, ns, p.num_seqs); };
+  auto layout = [&](int ns) {
+    return tc::smem_layout(p.d, pl.HG, pl.PPS, ns, p.num_seqs, window ? 1 : 0);
+  };
   int ns = 8;
-  while (ns > 2 && layout(ns).flag_off + 16 > (uint32_t)budget) --ns;
-  if (layout(ns).flag_off + 16 > (uint32_t)budget) return no("shared memory budget");
+  while (ns > 2 && layout(ns).total > (uint32_t)budget) --ns;
+  if (layout(ns).total > (uint32_t)budget) return no("shared memory budget");
   pl.NS = ns;
-  pl.smem = layout(ns).flag_off + 16 + 1024;
+  pl.smem = layout(ns).total + 1024;
   pl.ctas = sm_count;
-  const int rows_total = pl.HG * pl.MT * 16;
-  pl.part_floats = (size_t)rows_total * (p.d + 2);
+  const int unit_rows = pl.HG * per_head * 16;
+  pl.part_floats = (size_t)unit_rows * (p.d / 2 + 2);
   pl.part_floats = (pl.part_floats + 63) & ~(size_t)63;
-  const size_t part_bytes = (size_t)pl.ctas * pl.PPS * 2 * pl.part_floats * sizeof(float);
-  const size_t sem_bytes = (size_t)p.num_seqs * pl.NHG * pl.HG * pl.MT * sizeof(int32_t);
-  pl.ws_bytes = part_bytes + ((sem_bytes + 255) & ~(size_t)255);
+  pl.ws_bytes = tc::SEM_REGION + (size_t)pl.ctas * pl.PPS * 2 * pl.part_floats * sizeof(float);
   pl.ok = true;
   return pl;
 }
@@ -617,21 +687,19 @@ static int launch_tc_t(const AttnParams& p, const TcPlan& pl, void* ws, cudaStre
   P.NS = pl.NS;
   P.window = window ? 1 : 0;
   P.scale_log2 = p.scale * 1.4426950408889634f;
-  P.part = static_cast<float*>(ws);
-  const size_t part_bytes = (size_t)pl.ctas * pl.PPS * 2 * pl.part_floats * sizeof(float);
-  P.sems = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + part_bytes);
+  P.sems = static_cast<int32_t*>(ws);
+  P.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + tc::SEM_REGION);
   P.part_floats = (int)pl.part_floats;
   auto kern = tc::decode_kernel<T, D>;
   static thread_local int configured_dev = -1;
-  static thread_local size_t configured_smem = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_dev != dev || configured_smem < pl.smem) {
+  if (configured_dev != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
-    if (e != cudaSuccess) return fail(MF_ECUDA, std::string("paged attention: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess)
+      return fail(MF_ECUDA, std::string("paged attention: ") + cudaGetErrorString(e));
     configured_dev = dev;
-    configured_smem = 227 * 1024;
   }
   kern<<<pl.ctas, tc::THREADS, pl.smem, stream>>>(mk, mv, mwk, mwv, P);
   return check_launch("paged attention (tensor-core decode)");
@@ -640,10 +708,12 @@ static int launch_tc_t(const AttnParams& p, const TcPlan& pl, void* ws, cudaStre
 int launch_attn_tc(const AttnParams& p, mf_dtype dtype, const TcPlan& pl, void* ws,
                    cudaStream_t stream) {
   if (dtype == MF_BF16) {
-    if (p.d == 128) return launch_tc_t<__nv_bfloat16, 128>(p, pl, ws, stream, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    if (p.d == 128)
+      return launch_tc_t<__nv_bfloat16, 128>(p, pl, ws, stream, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
     return launch_tc_t<__nv_bfloat16, 64>(p, pl, ws, stream, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
   }
-  if (p.d == 128) return launch_tc_t<__half, 128>(p, pl, ws, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+  if (p.d == 128)
+    return launch_tc_t<__half, 128>(p, pl, ws, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
   return launch_tc_t<__half, 64>(p, pl, ws, stream, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
 }
 
@@ -667,16 +737,18 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// [tokens][heads][D] with D split into 64-element (128-byte) rows so that the
-// 128-byte swizzle applies; box = (64, D/64, HG, 16 tokens).
+// Tensor [tokens][heads][D] described as 4 dims, innermost first:
+// (64 elements, tokens, D/64 halves, heads) with strides (., tok, 128 B, head),
+// box (64, 16, D/64, HG): one page of HG heads lands in shared memory as
+// [HG][D/64][16 tokens][128 bytes], 128-byte swizzled.
 static CUresult encode_4d(CUtensorMap* map, const void* base, int D, int64_t stride_head_bytes,
                           int64_t stride_tok_bytes, int heads, int64_t tokens, int HG,
                           CUtensorMapDataType dt) {
   EncodeTiledFn fn = get_encode_fn();
   if (!fn) return CUDA_ERROR_NOT_SUPPORTED;
-  cuuint64_t dims[4] = {64, (cuuint64_t)(D / 64), (cuuint64_t)heads, (cuuint64_t)tokens};
-  cuuint64_t strides[3] = {128, (cuuint64_t)stride_head_bytes, (cuuint64_t)stride_tok_bytes};
-  cuuint32_t box[4] = {64, (cuuint32_t)(D / 64), (cuuint32_t)HG, (cuuint32_t)tc::PAGE};
+  cuuint64_t dims[4] = {64, (cuuint64_t)tokens, (cuuint64_t)(D / 64), (cuuint64_t)heads};
+  cuuint64_t strides[3] = {(cuuint64_t)stride_tok_bytes, 128, (cuuint64_t)stride_head_bytes};
+  cuuint32_t box[4] = {64, (cuuint32_t)tc::PAGE, (cuuint32_t)(D / 64), (cuuint32_t)HG};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
