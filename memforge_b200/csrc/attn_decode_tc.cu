@@ -155,11 +155,541 @@ MF_DEVINL void cursor_next(Cursor& c, const int* prefix, int B) {
   } while (c.pages == 0);
 }
 
+
+// State every consumer warp needs from the kernel prologue.
+struct Ctx {
+  const Params& P;
+  Smem L;
+  uint32_t base;
+  uint64_t* full;
+  uint64_t* empty;
+  volatile int* abort_flag;
+  const int* prefix;
+  int B;
+  int64_t T1, TP, NV;
+  int warp, lane, max_len;
+};
+
+// Partial slot layout, per virtual CTA and slot: acc[unit][RU rows][DU cols],
+// then m[unit][RU], then l[unit][RU] (unit_rows = units * RU).
+template <int RU, int DU>
+struct PartLayout {
+  const Params& P;
+  int unit_rows;
+  MF_DEVINL float* slot(int64_t vcx, int sl) const {
+    return P.part + (vcx * 2 + sl) * (int64_t)P.part_floats;
+  }
+  MF_DEVINL float* acc(float* s, int unit, int rr) const {
+    return s + (int64_t)(unit * RU + rr) * DU;
+  }
+  MF_DEVINL float* m(float* s, int unit) const { return s + (int64_t)unit_rows * DU + unit * RU; }
+  MF_DEVINL float* l(float* s, int unit) const { return m(s, unit) + unit_rows; }
+};
+
+// Merge every covering range's partial for one (sequence, head, unit) with the
+// log-sum-exp identity and write the output rows [row0, row0+RU) (columns
+// [col0, col0+DU) of the head).  Run by the warp whose arrival completed the set.
+template <typename T, int RU, int DU>
+MF_DEVINL void merge_unit(const Ctx& C, const PartLayout<RU, DU>& PL, int hg, int si, int hl,
+                          int unit, int row0, int col0) {
+  const Params& P = C.P;
+  const SeqGeo g = seq_geo(P, si);
+  const int head = hg * P.HG + hl;
+  const int64_t vstart = (int64_t)hg * C.T1 + C.prefix[si];
+  const int vc0 = owner(vstart, C.TP, C.NV);
+  const int vc1 = owner(vstart + g.pages - 1, C.TP, C.NV);
+  T* obase = static_cast<T*>(P.a.out);
+  __threadfence();
+  for (int rr = 0; rr < RU; ++rr) {
+    const int r = row0 + rr;
+    const int qi = r / P.G, gg = r % P.G;
+    if (qi >= g.q_len) continue;
+    float Mx = -INFINITY;
+    for (int c = vc0; c <= vc1; ++c) {
+      if (bound(c + 1, C.TP, C.NV) == bound(c, C.TP, C.NV)) continue;  // empty range
+      float* s = PL.slot(c, bound(c, C.TP, C.NV) >= vstart ? 0 : 1);
+      Mx = fmaxf(Mx, __ldcg(PL.m(s, unit) + rr));
+    }
+    const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
+    float Ls = 0.f;
+    float acc[DU / 32];
+#pragma unroll
+    for (int e = 0; e < DU / 32; ++e) acc[e] = 0.f;
+    for (int c = vc0; c <= vc1; ++c) {
+      if (bound(c + 1, C.TP, C.NV) == bound(c, C.TP, C.NV)) continue;
+      float* s = PL.slot(c, bound(c, C.TP, C.NV) >= vstart ? 0 : 1);
+      const float mk = __ldcg(PL.m(s, unit) + rr);
+      const float w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - Mu);
+      Ls += w * __ldcg(PL.l(s, unit) + rr);
+      const float* pa = PL.acc(s, unit, rr);
+#pragma unroll
+      for (int e = 0; e < DU / 32; ++e) acc[e] += w * __ldcg(pa + C.lane + 32 * e);
+    }
+    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+    T* orow = obase + (int64_t)map_row(P.a, g.q_start + qi) * P.a.o_sr +
+              (int64_t)(head * P.G + gg) * P.a.o_sh + col0;
+#pragma unroll
+    for (int e = 0; e < DU / 32; ++e) orow[C.lane + 32 * e] = from_f32<T>(acc[e] * inv);
+  }
+}
+
+// Arrival bookkeeping after a partial was written: true when this warp's
+// arrival completed the set of ranges covering the sequence.
+MF_DEVINL bool arrive_last(const Ctx& C, int32_t* sem, int hg, int si, int pages) {
+  __threadfence();
+  __syncwarp();
+  const int64_t vstart = (int64_t)hg * C.T1 + C.prefix[si];
+  const int vc0 = owner(vstart, C.TP, C.NV);
+  const int vc1 = owner(vstart + pages - 1, C.TP, C.NV);
+  // Ranges covering the sequence: [vc0, vc1] minus empty ones (a virtual CTA
+  // owns no page when there are fewer pages than ranges).
+  int covering = 0;
+  for (int c = vc0; c <= vc1; ++c) covering += bound(c + 1, C.TP, C.NV) > bound(c, C.TP, C.NV);
+  int old = 0;
+  if (C.lane == 0) old = atomicAdd(sem, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  return old == covering - 1;
+}
+
+// Wait for a stage; false (after flagging) when the wait gave up or another
+// warp aborted.
+MF_DEVINL bool wait_full(const Ctx& C, int stage, int it) {
+  if (!mbar_wait_bounded(&C.full[stage], (it / C.P.NS) & 1, WAIT_LIMIT)) {
+    if (C.lane == 0) set_err(C.P.a.err, MF_ERR_TIMEOUT);
+    *C.abort_flag = 1;
+  }
+  return !__any_sync(0xffffffffu, *C.abort_flag != 0);
+}
+
+MF_DEVINL void release(const Ctx& C, int stage) {
+  __syncwarp();
+  if (C.lane == 0) mbar_arrive(&C.empty[stage]);
+}
+
+MF_DEVINL uint32_t movm_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// -------------------------------------------------------------------------
+// Consumer for up to 8 query rows per kv head (decode): one warp per kv head.
+// S^T = K Q^T (M = 16 tokens, N = 8 rows, K = head_dim), P^T turned into the B
+// operand with movmatrix, O^T = V^T P^T (M = head_dim in 16-row tiles).
+// -------------------------------------------------------------------------
 template <typename T, int D>
+MF_DEVINL void consume_swapped(const Ctx& C) {
+  const Params& P = C.P;
+  using M = Mma<T>;
+  constexpr int RU = 8;
+  const int lane = C.lane;
+  const int units = P.HG;
+  const int hl = C.warp % units;          // local kv head
+  const int ps = C.warp / units;          // virtual CTA within this CTA
+  const int g4 = lane >> 2, c4 = lane & 3;
+  const int64_t vc = (int64_t)blockIdx.x * P.PPS + ps;
+  const int64_t lo = bound(vc, C.TP, C.NV);
+  const int len = (int)(bound(vc + 1, C.TP, C.NV) - lo);
+  const T* qbase = static_cast<const T*>(P.a.q);
+  T* obase = static_cast<T*>(P.a.out);
+  const float sl2 = P.scale_log2;
+  const PartLayout<RU, D> PL{P, units * RU};
+
+  int hg = 0, si = 0, k = 0, k0 = 0;
+  SeqGeo geo{};
+  bool first_piece = true;
+  int n_merge = 0, mhg0 = 0, msi0 = 0, mhg1 = 0, msi1 = 0;
+  uint32_t qb[D / 16][2];   // Q^T as the B operand: (k = dims, n = row g4)
+  float o[D / 16][4];       // O^T: (dims g4 / g4+8 of each 16-dim tile, rows 2c4, 2c4+1)
+  float mrow[2], lrow[2];   // rows 2c4, 2c4+1
+
+  for (int it = 0; it < C.max_len; ++it) {
+    const int stage = it % P.NS;
+    if (it >= len) {
+      release(C, stage);
+      continue;
+    }
+    if (it == 0 || k == geo.pages) {
+      const Cursor c = cursor_at(C.prefix, C.B, C.T1, lo + it);
+      hg = c.hg;
+      si = c.i;
+      k = c.k;
+      k0 = k;
+      geo = seq_geo(P, si);
+      const int head = hg * P.HG + hl;
+      const int qi = g4 / P.G, gg = g4 % P.G;
+      const bool valid = qi < geo.q_len;
+      const T* qrow = qbase + (valid ? (int64_t)map_row(P.a, geo.q_start + qi) * P.a.q_sr +
+                                           (int64_t)(head * P.G + gg) * P.a.q_sh
+                                     : 0);
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        qb[ks][0] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c4) : 0u;
+        qb[ks][1] = valid ? *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c4) : 0u;
+      }
+#pragma unroll
+      for (int n = 0; n < D / 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      mrow[0] = mrow[1] = -INFINITY;
+      lrow[0] = lrow[1] = 0.f;
+    }
+    if (!wait_full(C, stage, it)) return;
+
+    const uint32_t sK = C.base + stage * C.L.stage_bytes + ps * C.L.page_bytes;
+    const uint32_t sV = sK + P.PPS * C.L.page_bytes;
+    const bool is_win = P.window && k == geo.pool_pages;
+    const int kbase = is_win ? geo.pool_len : k * PAGE;
+    const int valid = is_win ? geo.q_len : min(PAGE, geo.pool_len - k * PAGE);
+    const int win_start = geo.kv_len - geo.q_len;
+    const bool need_mask = valid < PAGE || (P.a.causal && kbase + PAGE - 1 > win_start);
+
+    // S^T: two accumulators (even / odd k-steps) halve the dependent chain.
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t a[4];
+      const int tok = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int chunk = ks * 2 + (lane >> 4);
+      ldsm_x4(a[0], a[1], a[2], a[3], tile_addr<D>(sK, tok, hl, chunk));
+      M::run((ks & 1) ? s1 : s0, a, qb[ks][0], qb[ks][1]);
+    }
+    float sc[4];  // (tok g4, row 2c4), (tok g4, row 2c4+1), (tok g4+8, row 2c4), (tok g4+8, row 2c4+1)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float v = (s0[e] + s1[e]) * sl2;
+      if (need_mask) {
+        const int tok = g4 + 8 * (e >> 1);
+        const int r = 2 * c4 + (e & 1);
+        const int lim = P.a.causal ? win_start + r / P.G : geo.kv_len - 1;
+        if (tok >= valid || kbase + tok > lim) v = -INFINITY;
+      }
+      sc[e] = v;
+    }
+    uint32_t pb[2];  // P^T for tokens 0-7 / 8-15 as B fragments
+    float alpha[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float mx = fmaxf(sc[j], sc[2 + j]);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mnew = fmaxf(mrow[j], mx);
+      const float mu = (mnew == -INFINITY) ? 0.f : mnew;
+      alpha[j] = fast_exp2(mrow[j] - mu);
+      mrow[j] = mnew;
+      sc[j] = fast_exp2(sc[j] - mu);
+      sc[2 + j] = fast_exp2(sc[2 + j] - mu);
+      lrow[j] = lrow[j] * alpha[j] + (sc[j] + sc[2 + j]);
+    }
+    pb[0] = movm_trans(M::pack(sc[0], sc[1]));  // -> (row g4, tokens 2c4..2c4+1)
+    pb[1] = movm_trans(M::pack(sc[2], sc[3]));  // -> (row g4, tokens 8+2c4..)
+#pragma unroll
+    for (int n = 0; n < D / 16; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[1];
+      o[n][2] *= alpha[0];
+      o[n][3] *= alpha[1];
+    }
+    // O^T += V^T P^T, one 16-dim tile per mma
+#pragma unroll
+    for (int n = 0; n < D / 16; ++n) {
+      uint32_t a[4];
+      const int tok = (lane & 7) + ((lane >> 4) << 3);
+      const int chunk = n * 2 + ((lane >> 3) & 1);
+      ldsm_x4_trans(a[0], a[1], a[2], a[3], tile_addr<D>(sV, tok, hl, chunk));
+      if (valid < PAGE) {
+        // Unwritten slots may hold anything (NaN included): zero them.
+        const int t_lo = 2 * c4, t_hi = 8 + 2 * c4;
+        const uint32_t mlo = (t_lo < valid ? 0xffffu : 0u) | (t_lo + 1 < valid ? 0xffff0000u : 0u);
+        const uint32_t mhi = (t_hi < valid ? 0xffffu : 0u) | (t_hi + 1 < valid ? 0xffff0000u : 0u);
+        a[0] &= mlo;
+        a[1] &= mlo;
+        a[2] &= mhi;
+        a[3] &= mhi;
+      }
+      M::run(o[n], a, pb[0], pb[1]);
+    }
+    ++k;
+    release(C, stage);
+    if (k != geo.pages && it != len - 1) continue;
+
+    // ------------------------------------------------------ finish a piece
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      lrow[j] += __shfl_xor_sync(0xffffffffu, lrow[j], 4);
+      lrow[j] += __shfl_xor_sync(0xffffffffu, lrow[j], 8);
+      lrow[j] += __shfl_xor_sync(0xffffffffu, lrow[j], 16);
+    }
+    const int head = hg * P.HG + hl;
+    if (k0 == 0 && k == geo.pages) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = 2 * c4 + j;
+        const int qi = r / P.G, gg = r % P.G;
+        if (qi >= geo.q_len) continue;
+        const float inv = lrow[j] > 0.f ? 1.f / lrow[j] : 0.f;
+        T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
+                  (int64_t)(head * P.G + gg) * P.a.o_sh;
+#pragma unroll
+        for (int n = 0; n < D / 16; ++n) {
+          orow[n * 16 + g4] = from_f32<T>(o[n][j] * inv);
+          orow[n * 16 + 8 + g4] = from_f32<T>(o[n][2 + j] * inv);
+        }
+      }
+      first_piece = false;
+      continue;
+    }
+    float* sl = PL.slot(vc, first_piece ? 0 : 1);
+    first_piece = false;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      float* pa = PL.acc(sl, hl, 2 * c4 + j);
+#pragma unroll
+      for (int n = 0; n < D / 16; ++n) {
+        pa[n * 16 + g4] = o[n][j];
+        pa[n * 16 + 8 + g4] = o[n][2 + j];
+      }
+      if (g4 == 0) {
+        PL.m(sl, hl)[2 * c4 + j] = mrow[j];
+        PL.l(sl, hl)[2 * c4 + j] = lrow[j];
+      }
+    }
+    int32_t* sem = P.sems + (((int64_t)hg * C.B + si) * P.HG + hl);
+    if (!arrive_last(C, sem, hg, si, geo.pages)) continue;
+    if (n_merge == 0) {
+      mhg0 = hg;
+      msi0 = si;
+    } else {
+      mhg1 = hg;
+      msi1 = si;
+    }
+    ++n_merge;
+  }
+  for (int m = 0; m < n_merge; ++m) {
+    const int mhg = m == 0 ? mhg0 : mhg1;
+    const int msi = m == 0 ? msi0 : msi1;
+    merge_unit<T, RU, D>(C, PL, mhg, msi, hl, hl, 0, 0);
+    if (lane == 0) P.sems[((int64_t)mhg * C.B + msi) * P.HG + hl] = 0;
+  }
+}
+
+// -------------------------------------------------------------------------
+// Consumer for 9..64 query rows per kv head (speculative verify): warps own
+// (kv head, 16-row m-tile, half of head_dim); S = Q K^T in full, O[:, half] +=
+// P V.
+// -------------------------------------------------------------------------
+template <typename T, int D>
+MF_DEVINL void consume_split(const Ctx& C) {
+  const Params& P = C.P;
+  using M = Mma<T>;
+  constexpr int DH = D / 2;
+  constexpr int RU = 16;
+  const int lane = C.lane;
+  const int units = P.HG * P.MT * DS;
+  const int u = C.warp % units;
+  const int ps = C.warp / units;
+  const int dh = u % DS;
+  const int pair = u / DS;
+  const int mt = pair % P.MT;
+  const int hl = pair / P.MT;
+  const int unit = u;  // == (hl * MT + mt) * DS + dh
+  const int g4 = lane >> 2, c4 = lane & 3;
+  const int64_t vc = (int64_t)blockIdx.x * P.PPS + ps;
+  const int64_t lo = bound(vc, C.TP, C.NV);
+  const int len = (int)(bound(vc + 1, C.TP, C.NV) - lo);
+  const T* qbase = static_cast<const T*>(P.a.q);
+  T* obase = static_cast<T*>(P.a.out);
+  const float sl2 = P.scale_log2;
+  const PartLayout<RU, DH> PL{P, units * RU};
+
+  int hg = 0, si = 0, k = 0, k0 = 0;
+  SeqGeo geo{};
+  bool first_piece = true;
+  int n_merge = 0, mhg0 = 0, msi0 = 0, mhg1 = 0, msi1 = 0;
+  uint32_t qf[D / 16][4];
+  float o[DH / 8][4];
+  float mrow[2], lrow[2];
+
+  for (int it = 0; it < C.max_len; ++it) {
+    const int stage = it % P.NS;
+    if (it >= len) {
+      release(C, stage);
+      continue;
+    }
+    if (it == 0 || k == geo.pages) {
+      const Cursor c = cursor_at(C.prefix, C.B, C.T1, lo + it);
+      hg = c.hg;
+      si = c.i;
+      k = c.k;
+      k0 = k;
+      geo = seq_geo(P, si);
+      const int head = hg * P.HG + hl;
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int r = mt * 16 + g4 + 8 * h2;
+        const int qi = r / P.G, gg = r % P.G;
+        const bool valid = qi < geo.q_len;
+        const T* qrow = qbase + (valid ? (int64_t)map_row(P.a, geo.q_start + qi) * P.a.q_sr +
+                                             (int64_t)(head * P.G + gg) * P.a.q_sh
+                                       : 0);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          uint32_t lo32 = 0, hi32 = 0;
+          if (valid) {
+            lo32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c4);
+            hi32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c4);
+          }
+          qf[ks][h2] = lo32;      // rows g / g+8, k 0..7 of the step
+          qf[ks][2 + h2] = hi32;  // rows g / g+8, k 8..15
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < DH / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+      mrow[0] = mrow[1] = -INFINITY;
+      lrow[0] = lrow[1] = 0.f;
+    }
+    if (!wait_full(C, stage, it)) return;
+
+    const uint32_t sK = C.base + stage * C.L.stage_bytes + ps * C.L.page_bytes;
+    const uint32_t sV = sK + P.PPS * C.L.page_bytes;
+    const bool is_win = P.window && k == geo.pool_pages;
+    const int kbase = is_win ? geo.pool_len : k * PAGE;
+    const int valid = is_win ? geo.q_len : min(PAGE, geo.pool_len - k * PAGE);
+    const int win_start = geo.kv_len - geo.q_len;
+    const bool need_mask = valid < PAGE || (P.a.causal && kbase + PAGE - 1 > win_start);
+
+    float sc[2][4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t b0, b1, b2, b3;
+      const int tok = (lane & 7) + ((lane >> 4) << 3);
+      const int chunk = ks * 2 + ((lane >> 3) & 1);
+      ldsm_x4(b0, b1, b2, b3, tile_addr<D>(sK, tok, hl, chunk));
+      M::run(sc[0], qf[ks], b0, b1);
+      M::run(sc[1], qf[ks], b2, b3);
+    }
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float s = sc[n][e] * sl2;
+        if (need_mask) {
+          const int tok = n * 8 + 2 * c4 + (e & 1);
+          const int r = mt * 16 + g4 + 8 * (e >> 1);
+          const int lim = P.a.causal ? win_start + r / P.G : geo.kv_len - 1;
+          if (tok >= valid || kbase + tok > lim) s = -INFINITY;
+        }
+        sc[n][e] = s;
+        mx[e >> 1] = fmaxf(mx[e >> 1], s);
+      }
+    }
+    uint32_t pa[4];
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 1));
+      mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 2));
+      const float mnew = fmaxf(mrow[h2], mx[h2]);
+      const float mu = (mnew == -INFINITY) ? 0.f : mnew;
+      const float alpha = fast_exp2(mrow[h2] - mu);
+      mrow[h2] = mnew;
+      const float p0 = fast_exp2(sc[0][2 * h2] - mu), p1 = fast_exp2(sc[0][2 * h2 + 1] - mu);
+      const float p2 = fast_exp2(sc[1][2 * h2] - mu), p3 = fast_exp2(sc[1][2 * h2 + 1] - mu);
+      lrow[h2] = lrow[h2] * alpha + (p0 + p1 + p2 + p3);
+#pragma unroll
+      for (int n = 0; n < DH / 8; ++n) {
+        o[n][2 * h2] *= alpha;
+        o[n][2 * h2 + 1] *= alpha;
+      }
+      pa[h2] = M::pack(p0, p1);
+      pa[2 + h2] = M::pack(p2, p3);
+    }
+#pragma unroll
+    for (int np = 0; np < DH / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      const int tok = (lane & 7) + (((lane >> 3) & 1) << 3);
+      const int chunk = dh * (DH / 8) + np * 2 + (lane >> 4);
+      ldsm_x4_trans(b0, b1, b2, b3, tile_addr<D>(sV, tok, hl, chunk));
+      if (valid < PAGE) {
+        const int t_lo = 2 * c4, t_hi = 8 + 2 * c4;
+        const uint32_t mlo = (t_lo < valid ? 0xffffu : 0u) | (t_lo + 1 < valid ? 0xffff0000u : 0u);
+        const uint32_t mhi = (t_hi < valid ? 0xffffu : 0u) | (t_hi + 1 < valid ? 0xffff0000u : 0u);
+        b0 &= mlo;
+        b1 &= mhi;
+        b2 &= mlo;
+        b3 &= mhi;
+      }
+      M::run(o[2 * np], pa, b0, b1);
+      M::run(o[2 * np + 1], pa, b2, b3);
+    }
+    ++k;
+    release(C, stage);
+    if (k != geo.pages && it != len - 1) continue;
+
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      lrow[h2] += __shfl_xor_sync(0xffffffffu, lrow[h2], 1);
+      lrow[h2] += __shfl_xor_sync(0xffffffffu, lrow[h2], 2);
+    }
+    const int head = hg * P.HG + hl;
+    if (k0 == 0 && k == geo.pages) {
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int r = mt * 16 + g4 + 8 * h2;
+        const int qi = r / P.G, gg = r % P.G;
+        if (qi >= geo.q_len) continue;
+        const float inv = lrow[h2] > 0.f ? 1.f / lrow[h2] : 0.f;
+        T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
+                  (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
+#pragma unroll
+        for (int n = 0; n < DH / 8; ++n) {
+          *reinterpret_cast<uint32_t*>(orow + n * 8 + 2 * c4) =
+              M::pack(o[n][2 * h2] * inv, o[n][2 * h2 + 1] * inv);
+        }
+      }
+      first_piece = false;
+      continue;
+    }
+    float* sl = PL.slot(vc, first_piece ? 0 : 1);
+    first_piece = false;
+#pragma unroll
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int rr = g4 + 8 * h2;
+      float* pacc = PL.acc(sl, unit, rr);
+#pragma unroll
+      for (int n = 0; n < DH / 8; ++n)
+        *reinterpret_cast<float2*>(pacc + n * 8 + 2 * c4) =
+            make_float2(o[n][2 * h2], o[n][2 * h2 + 1]);
+      if (c4 == 0) {
+        PL.m(sl, unit)[rr] = mrow[h2];
+        PL.l(sl, unit)[rr] = lrow[h2];
+      }
+    }
+    int32_t* sem = P.sems + ((int64_t)hg * C.B + si) * units + unit;
+    if (!arrive_last(C, sem, hg, si, geo.pages)) continue;
+    if (n_merge == 0) {
+      mhg0 = hg;
+      msi0 = si;
+    } else {
+      mhg1 = hg;
+      msi1 = si;
+    }
+    ++n_merge;
+  }
+  for (int m = 0; m < n_merge; ++m) {
+    const int mhg = m == 0 ? mhg0 : mhg1;
+    const int msi = m == 0 ? msi0 : msi1;
+    merge_unit<T, RU, DH>(C, PL, mhg, msi, hl, unit, mt * 16, dh * DH);
+    if (lane == 0) P.sems[((int64_t)mhg * C.B + msi) * units + unit] = 0;
+  }
+}
+
+template <typename T, int D, bool SW>
 __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
     const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
     const __grid_constant__ CUtensorMap twk, const __grid_constant__ CUtensorMap twv,
-    const Params P) {
+    const __grid_constant__ Params P) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -173,8 +703,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L.flag_off);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int units = P.HG * P.MT * DS;      // consumer units per page
-  const int active_warps = units * P.PPS;  // consumer warps with work
+  const int units = SW ? P.HG : P.HG * P.MT * DS;  // consumer warps per page
+  const int active_warps = units * P.PPS;          // consumer warps with work
 
   // ---------------------------------------------------------------- prologue
   if (tid == 0) {
@@ -311,283 +841,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
 
   // ============================================================== consumers
   if (warp >= active_warps) return;
-  using M = Mma<T>;
-  constexpr int DH = D / 2;          // head_dim columns this warp accumulates
-  const int u = warp % units;
-  const int ps = warp / units;       // virtual CTA within this CTA
-  const int dh = u % DS;             // which half of head_dim
-  const int pair = u / DS;
-  const int mt = pair % P.MT;        // m-tile
-  const int hl = pair / P.MT;        // local kv head
-  const int g4 = lane >> 2, c4 = lane & 3;
-  const int64_t vc = (int64_t)blockIdx.x * P.PPS + ps;
-  const int64_t lo = bound(vc, TP, NV);
-  const int len = (int)(bound(vc + 1, TP, NV) - lo);
-  const T* qbase = static_cast<const T*>(P.a.q);
-  T* obase = static_cast<T*>(P.a.out);
-  const float sl2 = P.scale_log2;
-
-  int hg = 0, si = 0, k = 0, k0 = 0;
-  SeqGeo geo{};
-  bool first_piece = true;
-  int n_merge = 0, merge_hg0 = 0, merge_si0 = 0, merge_hg1 = 0, merge_si1 = 0;
-  uint32_t qf[D / 16][4];
-  float o[DH / 8][4];
-  float mrow[2], lrow[2];
-
-  for (int it = 0; it < max_len; ++it) {
-    const int stage = it % P.NS;
-    if (it >= len) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
-      continue;
-    }
-    if (it == 0 || k == geo.pages) {
-      // ---------------------------------------------------- start a piece
-      const Cursor c = cursor_at(prefix, B, T1, lo + it);
-      hg = c.hg;
-      si = c.i;
-      k = c.k;
-      k0 = k;
-      geo = seq_geo(P, si);
-      const int head = hg * P.HG + hl;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int r = mt * 16 + g4 + 8 * h2;
-        const int qi = r / P.G, gg = r % P.G;
-        const bool valid = qi < geo.q_len;
-        const T* qrow = qbase + (valid ? (int64_t)map_row(P.a, geo.q_start + qi) * P.a.q_sr +
-                                             (int64_t)(head * P.G + gg) * P.a.q_sh
-                                       : 0);
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          uint32_t lo32 = 0, hi32 = 0;
-          if (valid) {
-            lo32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 2 * c4);
-            hi32 = *reinterpret_cast<const uint32_t*>(qrow + ks * 16 + 8 + 2 * c4);
-          }
-          qf[ks][h2] = lo32;      // rows g / g+8, k 0..7 of the step
-          qf[ks][2 + h2] = hi32;  // rows g / g+8, k 8..15
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < DH / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-      mrow[0] = mrow[1] = -INFINITY;
-      lrow[0] = lrow[1] = 0.f;
-    }
-
-    if (!mbar_wait_bounded(&full[stage], (it / P.NS) & 1, WAIT_LIMIT)) {
-      if (lane == 0) set_err(P.a.err, MF_ERR_TIMEOUT);
-      *abort_flag = 1;
-    }
-    if (__any_sync(0xffffffffu, *abort_flag != 0)) return;
-
-    const uint32_t sK = base + stage * L.stage_bytes + ps * L.page_bytes;
-    const uint32_t sV = sK + P.PPS * L.page_bytes;
-    const bool is_win = P.window && k == geo.pool_pages;
-    const int kbase = is_win ? geo.pool_len : k * PAGE;
-    const int valid = is_win ? geo.q_len : min(PAGE, geo.pool_len - k * PAGE);
-    const int win_start = geo.kv_len - geo.q_len;
-    const bool need_mask = valid < PAGE || (P.a.causal && kbase + PAGE - 1 > win_start);
-
-    // S = Q K^T for 16 rows x 16 tokens (full head_dim)
-    float sc[2][4];
-#pragma unroll
-    for (int n = 0; n < 2; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < D / 16; ++ks) {
-      uint32_t b0, b1, b2, b3;
-      const int tok = (lane & 7) + ((lane >> 4) << 3);
-      const int chunk = ks * 2 + ((lane >> 3) & 1);
-      ldsm_x4(b0, b1, b2, b3, tile_addr<D>(sK, tok, hl, chunk));
-      M::run(sc[0], qf[ks], b0, b1);
-      M::run(sc[1], qf[ks], b2, b3);
-    }
-    // online softmax (log2 domain)
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < 2; ++n) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float s = sc[n][e] * sl2;
-        if (need_mask) {
-          const int tok = n * 8 + 2 * c4 + (e & 1);
-          const int r = mt * 16 + g4 + 8 * (e >> 1);
-          const int lim = P.a.causal ? win_start + r / P.G : geo.kv_len - 1;
-          if (tok >= valid || kbase + tok > lim) s = -INFINITY;
-        }
-        sc[n][e] = s;
-        mx[e >> 1] = fmaxf(mx[e >> 1], s);
-      }
-    }
-    uint32_t pa[4];
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 1));
-      mx[h2] = fmaxf(mx[h2], __shfl_xor_sync(0xffffffffu, mx[h2], 2));
-      const float mnew = fmaxf(mrow[h2], mx[h2]);
-      const float mu = (mnew == -INFINITY) ? 0.f : mnew;
-      const float alpha = fast_exp2(mrow[h2] - mu);
-      mrow[h2] = mnew;
-      const float p0 = fast_exp2(sc[0][2 * h2] - mu), p1 = fast_exp2(sc[0][2 * h2 + 1] - mu);
-      const float p2 = fast_exp2(sc[1][2 * h2] - mu), p3 = fast_exp2(sc[1][2 * h2 + 1] - mu);
-      lrow[h2] = lrow[h2] * alpha + (p0 + p1 + p2 + p3);
-#pragma unroll
-      for (int n = 0; n < DH / 8; ++n) {
-        o[n][2 * h2] *= alpha;
-        o[n][2 * h2 + 1] *= alpha;
-      }
-      pa[h2] = M::pack(p0, p1);      // rows g / g+8, tokens 2c..2c+1
-      pa[2 + h2] = M::pack(p2, p3);  // rows g / g+8, tokens 8+2c..
-    }
-    // O[:, dh half] += P V
-#pragma unroll
-    for (int np = 0; np < DH / 16; ++np) {
-      uint32_t b0, b1, b2, b3;
-      const int tok = (lane & 7) + (((lane >> 3) & 1) << 3);
-      const int chunk = dh * (DH / 8) + np * 2 + (lane >> 4);
-      ldsm_x4_trans(b0, b1, b2, b3, tile_addr<D>(sV, tok, hl, chunk));
-      if (valid < PAGE) {
-        // Unwritten slots may hold anything (NaN included): zero them so that
-        // p = 0 really contributes nothing.
-        const int t_lo = 2 * c4, t_hi = 8 + 2 * c4;
-        const uint32_t mlo = (t_lo < valid ? 0xffffu : 0u) | (t_lo + 1 < valid ? 0xffff0000u : 0u);
-        const uint32_t mhi = (t_hi < valid ? 0xffffu : 0u) | (t_hi + 1 < valid ? 0xffff0000u : 0u);
-        b0 &= mlo;
-        b1 &= mhi;
-        b2 &= mlo;
-        b3 &= mhi;
-      }
-      M::run(o[2 * np], pa, b0, b1);
-      M::run(o[2 * np + 1], pa, b2, b3);
-    }
-    ++k;
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[stage]);
-
-    if (k != geo.pages && it != len - 1) continue;
-    // ------------------------------------------------------ finish a piece
-#pragma unroll
-    for (int h2 = 0; h2 < 2; ++h2) {
-      lrow[h2] += __shfl_xor_sync(0xffffffffu, lrow[h2], 1);
-      lrow[h2] += __shfl_xor_sync(0xffffffffu, lrow[h2], 2);
-    }
-    const int head = hg * P.HG + hl;
-    if (k0 == 0 && k == geo.pages) {
-      // The piece is the whole sequence: write the output rows directly.
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int r = mt * 16 + g4 + 8 * h2;
-        const int qi = r / P.G, gg = r % P.G;
-        if (qi >= geo.q_len) continue;
-        const float inv = lrow[h2] > 0.f ? 1.f / lrow[h2] : 0.f;
-        T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
-                  (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
-#pragma unroll
-        for (int n = 0; n < DH / 8; ++n) {
-          *reinterpret_cast<uint32_t*>(orow + n * 8 + 2 * c4) =
-              M::pack(o[n][2 * h2] * inv, o[n][2 * h2 + 1] * inv);
-        }
-      }
-      first_piece = false;
-      continue;
-    }
-    // Partial: slot 0 when this piece starts the virtual CTA's range.
-    const int slot = first_piece ? 0 : 1;
-    first_piece = false;
-    const int unit = (hl * P.MT + mt) * DS + dh;
-    const int unit_rows = P.HG * P.MT * DS * 16;
-    {
-      float* part = P.part + (vc * 2 + slot) * (int64_t)P.part_floats;
-      float* pacc = part + (int64_t)(unit * 16) * DH;
-      float* pm = part + (int64_t)unit_rows * DH + unit * 16;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int rr = g4 + 8 * h2;
-#pragma unroll
-        for (int n = 0; n < DH / 8; ++n)
-          *reinterpret_cast<float2*>(pacc + rr * DH + n * 8 + 2 * c4) =
-              make_float2(o[n][2 * h2], o[n][2 * h2 + 1]);
-        if (c4 == 0) {
-          pm[rr] = mrow[h2];
-          pm[unit_rows + rr] = lrow[h2];
-        }
-      }
-    }
-    __threadfence();
-    __syncwarp();
-    const int64_t vstart = (int64_t)hg * T1 + prefix[si];
-    const int64_t vend = vstart + geo.pages;
-    const int vc0 = owner(vstart, TP, NV);
-    const int vc1 = owner(vend - 1, TP, NV);
-    // Ranges covering this sequence: [vc0, vc1] minus empty ones (a virtual CTA
-    // owns no page when there are fewer pages than ranges).
-    int covering = 0;
-    for (int c = vc0; c <= vc1; ++c) covering += bound(c + 1, TP, NV) > bound(c, TP, NV);
-    int32_t* sem = P.sems + (((int64_t)hg * B + si) * P.HG + hl) * (P.MT * DS) + mt * DS + dh;
-    int old = 0;
-    if (lane == 0) old = atomicAdd(sem, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old != covering - 1) continue;
-    // Last arrival for this (sequence, head, m-tile, half): merge after the
-    // streaming loop (at most two per virtual CTA: its first and last piece).
-    if (n_merge == 0) {
-      merge_hg0 = hg;
-      merge_si0 = si;
-    } else {
-      merge_hg1 = hg;
-      merge_si1 = si;
-    }
-    ++n_merge;
-  }
-
-  for (int m = 0; m < n_merge; ++m) {
-    const int mhg = m == 0 ? merge_hg0 : merge_hg1;
-    const int msi = m == 0 ? merge_si0 : merge_si1;
-    const SeqGeo mg = seq_geo(P, msi);
-    const int head = mhg * P.HG + hl;
-    const int unit = (hl * P.MT + mt) * DS + dh;
-    const int unit_rows = P.HG * P.MT * DS * 16;
-    const int64_t vstart = (int64_t)mhg * T1 + prefix[msi];
-    const int vc0 = owner(vstart, TP, NV);
-    const int vc1 = owner(vstart + mg.pages - 1, TP, NV);
-    int32_t* sem = P.sems + (((int64_t)mhg * B + msi) * P.HG + hl) * (P.MT * DS) + mt * DS + dh;
-    __threadfence();
-    for (int rr = 0; rr < 16; ++rr) {
-      const int r = mt * 16 + rr;
-      const int qi = r / P.G, gg = r % P.G;
-      if (qi >= mg.q_len) continue;
-      float Mx = -INFINITY;
-      for (int c = vc0; c <= vc1; ++c) {
-        if (bound(c + 1, TP, NV) == bound(c, TP, NV)) continue;  // empty range
-        const int sl = (bound(c, TP, NV) >= vstart) ? 0 : 1;
-        const float* pp = P.part + (int64_t)(c * 2 + sl) * P.part_floats;
-        Mx = fmaxf(Mx, __ldcg(pp + (int64_t)unit_rows * DH + unit * 16 + rr));
-      }
-      const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
-      float Ls = 0.f;
-      float acc[DH / 32];
-#pragma unroll
-      for (int e = 0; e < DH / 32; ++e) acc[e] = 0.f;
-      for (int c = vc0; c <= vc1; ++c) {
-        if (bound(c + 1, TP, NV) == bound(c, TP, NV)) continue;
-        const int sl = (bound(c, TP, NV) >= vstart) ? 0 : 1;
-        const float* pp = P.part + (int64_t)(c * 2 + sl) * P.part_floats;
-        const float mk = __ldcg(pp + (int64_t)unit_rows * DH + unit * 16 + rr);
-        const float w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - Mu);
-        Ls += w * __ldcg(pp + (int64_t)unit_rows * DH + unit_rows + unit * 16 + rr);
-        const float* pa2 = pp + (int64_t)(unit * 16 + rr) * DH;
-#pragma unroll
-        for (int e = 0; e < DH / 32; ++e) acc[e] += w * __ldcg(pa2 + lane + 32 * e);
-      }
-      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-      T* orow = obase + (int64_t)map_row(P.a, mg.q_start + qi) * P.a.o_sr +
-                (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
-#pragma unroll
-      for (int e = 0; e < DH / 32; ++e) orow[lane + 32 * e] = from_f32<T>(acc[e] * inv);
-    }
-    if (lane == 0) *sem = 0;  // leave the counter zeroed for the next launch
-  }
+  Ctx C{P, L, base, full, empty, abort_flag, prefix, B, T1, TP, NV, warp, lane, max_len};
+  if constexpr (SW)
+    consume_swapped<T, D>(C);
+  else
+    consume_split<T, D>(C);
 }
 
 }  // namespace tc
@@ -622,8 +880,9 @@ TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool wind
       return no("window base not 16-byte aligned");
     if (p.row_map) return no("window with row_map");
   }
+  pl.SW = rows <= 8;
   pl.MT = (rows + 15) / 16;
-  const int per_head = pl.MT * tc::DS;
+  const int per_head = pl.SW ? 1 : pl.MT * tc::DS;  // consumer warps per kv head
   const int cap = tc::CONSUMER_WARPS / per_head;
   pl.HG = 1;
   for (int hg = cap; hg >= 1; --hg)
@@ -646,8 +905,10 @@ TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool wind
   pl.NS = ns;
   pl.smem = layout(ns).total + 1024;
   pl.ctas = sm_count;
-  const int unit_rows = pl.HG * per_head * 16;
-  pl.part_floats = (size_t)unit_rows * (p.d / 2 + 2);
+  // partial slot: per unit RU rows x DU columns of fp32 plus m and l per row
+  const int ru = pl.SW ? 8 : 16, du = pl.SW ? p.d : p.d / 2;
+  const int unit_rows = pl.HG * per_head * ru;
+  pl.part_floats = (size_t)unit_rows * (du + 2);
   pl.part_floats = (pl.part_floats + 63) & ~(size_t)63;
   pl.ws_bytes = tc::SEM_REGION + (size_t)pl.ctas * pl.PPS * 2 * pl.part_floats * sizeof(float);
   pl.ok = true;
@@ -690,16 +951,16 @@ static int launch_tc_t(const AttnParams& p, const TcPlan& pl, void* ws, cudaStre
   P.sems = static_cast<int32_t*>(ws);
   P.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + tc::SEM_REGION);
   P.part_floats = (int)pl.part_floats;
-  auto kern = tc::decode_kernel<T, D>;
-  static thread_local int configured_dev = -1;
+  auto kern = pl.SW ? tc::decode_kernel<T, D, true> : tc::decode_kernel<T, D, false>;
+  static thread_local int configured_dev[2] = {-1, -1};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (configured_dev != dev) {
+  if (configured_dev[pl.SW] != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024);
     if (e != cudaSuccess)
       return fail(MF_ECUDA, std::string("paged attention: ") + cudaGetErrorString(e));
-    configured_dev = dev;
+    configured_dev[pl.SW] = dev;
   }
   kern<<<pl.ctas, tc::THREADS, pl.smem, stream>>>(mk, mv, mwk, mwv, P);
   return check_launch("paged attention (tensor-core decode)");

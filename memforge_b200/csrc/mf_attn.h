@@ -50,6 +50,7 @@ int launch_attn_generic(const AttnParams& p, mf_dtype dtype, cudaStream_t stream
 struct TcPlan {
   bool ok = false;
   const char* why = "";
+  bool SW = false;  // swapped-operand decode consumer (<= 8 rows per kv head)
   int MT = 1, HG = 1, NHG = 1, PPS = 1, NS = 2, ctas = 0;
   size_t smem = 0;
   size_t part_floats = 0;   // floats per partial slot
