@@ -188,48 +188,111 @@ struct PartLayout {
 
 // Merge every covering range's partial for one (sequence, head, unit) with the
 // log-sum-exp identity and write the output rows [row0, row0+RU) (columns
-// [col0, col0+DU) of the head).  Run by the warp whose arrival completed the set.
+// [col0, col0+DU) of the head).  Run by the warp whose arrival completed the
+// set.  Latency-bound, so every load of a pass is independent: lane l first
+// reads (m, l) of (range l / RU, row l % RU) for 32/RU ranges at once, then
+// every lane reads its columns of all rows of those ranges.
 template <typename T, int RU, int DU>
 MF_DEVINL void merge_unit(const Ctx& C, const PartLayout<RU, DU>& PL, int hg, int si, int hl,
                           int unit, int row0, int col0) {
+  constexpr int RPP = 32 / RU;  // ranges per pass
   const Params& P = C.P;
+  const int lane = C.lane;
   const SeqGeo g = seq_geo(P, si);
   const int head = hg * P.HG + hl;
   const int64_t vstart = (int64_t)hg * C.T1 + C.prefix[si];
   const int vc0 = owner(vstart, C.TP, C.NV);
   const int vc1 = owner(vstart + g.pages - 1, C.TP, C.NV);
-  T* obase = static_cast<T*>(P.a.out);
   __threadfence();
-  for (int rr = 0; rr < RU; ++rr) {
-    const int r = row0 + rr;
-    const int qi = r / P.G, gg = r % P.G;
+  float Mrun[RU], acc[RU][DU / 32], Lrun = 0.f;  // Lrun: row lane % RU
+#pragma unroll
+  for (int r = 0; r < RU; ++r) {
+    Mrun[r] = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < DU / 32; ++e) acc[r][e] = 0.f;
+  }
+  int c = vc0;
+  while (c <= vc1) {
+    // Gather up to RPP non-empty ranges.
+    float* slots[RPP];
+    int n = 0;
+#pragma unroll
+    for (int j = 0; j < RPP; ++j) slots[j] = nullptr;
+    while (c <= vc1 && n < RPP) {
+      if (bound(c + 1, C.TP, C.NV) > bound(c, C.TP, C.NV)) {
+#pragma unroll
+        for (int j = 0; j < RPP; ++j)
+          if (j == n) slots[j] = PL.slot(c, bound(c, C.TP, C.NV) >= vstart ? 0 : 1);
+        ++n;
+      }
+      ++c;
+    }
+    // Pass 1: (m, l) of (range lane / RU, row lane % RU).
+    const int my_r = lane % RU, my_j = lane / RU;
+    float mk = -INFINITY, lk = 0.f;
+#pragma unroll
+    for (int j = 0; j < RPP; ++j)
+      if (j == my_j && j < n) {
+        mk = __ldcg(PL.m(slots[j], unit) + my_r);
+        lk = __ldcg(PL.l(slots[j], unit) + my_r);
+      }
+    float mx = mk;
+#pragma unroll
+    for (int o = RU; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    // New running max of every row, and the factor for what was accumulated so far.
+    float Mr_new[RU], scale_old[RU];
+#pragma unroll
+    for (int r = 0; r < RU; ++r) {
+      const float mxr = __shfl_sync(0xffffffffu, mx, r);  // lane r holds row r's pass max
+      Mr_new[r] = fmaxf(Mrun[r], mxr);
+      const float mu = Mr_new[r] == -INFINITY ? 0.f : Mr_new[r];
+      scale_old[r] = Mrun[r] == -INFINITY ? 0.f : fast_exp2(Mrun[r] - mu);
+    }
+    float w;
+    {
+      float mu_mine = 0.f, so_mine = 0.f;
+#pragma unroll
+      for (int r = 0; r < RU; ++r)
+        if (r == my_r) {
+          mu_mine = Mr_new[r] == -INFINITY ? 0.f : Mr_new[r];
+          so_mine = scale_old[r];
+        }
+      w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - mu_mine);
+      float lw = w * lk;
+#pragma unroll
+      for (int o = RU; o < 32; o <<= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+      Lrun = Lrun * so_mine + lw;  // lanes with equal lane % RU agree
+    }
+    // Pass 2: every lane accumulates its columns of every row.
+#pragma unroll
+    for (int r = 0; r < RU; ++r) {
+#pragma unroll
+      for (int e = 0; e < DU / 32; ++e) acc[r][e] *= scale_old[r];
+      Mrun[r] = Mr_new[r];
+    }
+#pragma unroll
+    for (int j = 0; j < RPP; ++j) {
+      if (j >= n) break;
+#pragma unroll
+      for (int r = 0; r < RU; ++r) {
+        const float wj = __shfl_sync(0xffffffffu, w, j * RU + r);
+        const float* pa = PL.acc(slots[j], unit, r);
+#pragma unroll
+        for (int e = 0; e < DU / 32; ++e) acc[r][e] += wj * __ldcg(pa + lane + 32 * e);
+      }
+    }
+  }
+  T* obase = static_cast<T*>(P.a.out);
+#pragma unroll
+  for (int r = 0; r < RU; ++r) {
+    const float Lr = __shfl_sync(0xffffffffu, Lrun, r);
+    const int qi = (row0 + r) / P.G, gg = (row0 + r) % P.G;
     if (qi >= g.q_len) continue;
-    float Mx = -INFINITY;
-    for (int c = vc0; c <= vc1; ++c) {
-      if (bound(c + 1, C.TP, C.NV) == bound(c, C.TP, C.NV)) continue;  // empty range
-      float* s = PL.slot(c, bound(c, C.TP, C.NV) >= vstart ? 0 : 1);
-      Mx = fmaxf(Mx, __ldcg(PL.m(s, unit) + rr));
-    }
-    const float Mu = (Mx == -INFINITY) ? 0.f : Mx;
-    float Ls = 0.f;
-    float acc[DU / 32];
-#pragma unroll
-    for (int e = 0; e < DU / 32; ++e) acc[e] = 0.f;
-    for (int c = vc0; c <= vc1; ++c) {
-      if (bound(c + 1, C.TP, C.NV) == bound(c, C.TP, C.NV)) continue;
-      float* s = PL.slot(c, bound(c, C.TP, C.NV) >= vstart ? 0 : 1);
-      const float mk = __ldcg(PL.m(s, unit) + rr);
-      const float w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - Mu);
-      Ls += w * __ldcg(PL.l(s, unit) + rr);
-      const float* pa = PL.acc(s, unit, rr);
-#pragma unroll
-      for (int e = 0; e < DU / 32; ++e) acc[e] += w * __ldcg(pa + C.lane + 32 * e);
-    }
-    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+    const float inv = Lr > 0.f ? 1.f / Lr : 0.f;
     T* orow = obase + (int64_t)map_row(P.a, g.q_start + qi) * P.a.o_sr +
               (int64_t)(head * P.G + gg) * P.a.o_sh + col0;
 #pragma unroll
-    for (int e = 0; e < DU / 32; ++e) orow[C.lane + 32 * e] = from_f32<T>(acc[e] * inv);
+    for (int e = 0; e < DU / 32; ++e) orow[lane + 32 * e] = from_f32<T>(acc[r][e] * inv);
   }
 }
 
@@ -253,8 +316,8 @@ MF_DEVINL bool arrive_last(const Ctx& C, int32_t* sem, int hg, int si, int pages
 
 // Wait for a stage; false (after flagging) when the wait gave up or another
 // warp aborted.
-MF_DEVINL bool wait_full(const Ctx& C, int stage, int it) {
-  if (!mbar_wait_bounded(&C.full[stage], (it / C.P.NS) & 1, WAIT_LIMIT)) {
+MF_DEVINL bool wait_full(const Ctx& C, int stage, uint32_t phase) {
+  if (!mbar_wait_bounded(&C.full[stage], phase, WAIT_LIMIT)) {
     if (C.lane == 0) set_err(C.P.a.err, MF_ERR_TIMEOUT);
     *C.abort_flag = 1;
   }
@@ -293,6 +356,9 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
   const T* qbase = static_cast<const T*>(P.a.q);
   T* obase = static_cast<T*>(P.a.out);
   const float sl2 = P.scale_log2;
+  const int NS = P.NS, G = P.G, causal = P.a.causal, window = P.window;
+  const uint32_t stage_bytes = C.L.stage_bytes, page_bytes = C.L.page_bytes;
+  const uint32_t v_off = P.PPS * page_bytes;
   const PartLayout<RU, D> PL{P, units * RU};
 
   int hg = 0, si = 0, k = 0, k0 = 0;
@@ -303,8 +369,10 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
   float o[D / 16][4];       // O^T: (dims g4 / g4+8 of each 16-dim tile, rows 2c4, 2c4+1)
   float mrow[2], lrow[2];   // rows 2c4, 2c4+1
 
-  for (int it = 0; it < C.max_len; ++it) {
-    const int stage = it % P.NS;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int it = 0; it < C.max_len; ++it, stage = (stage + 1 == NS) ? 0 : stage + 1,
+           phase ^= (stage == 0) ? 1u : 0u) {
     if (it >= len) {
       release(C, stage);
       continue;
@@ -332,15 +400,15 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
       mrow[0] = mrow[1] = -INFINITY;
       lrow[0] = lrow[1] = 0.f;
     }
-    if (!wait_full(C, stage, it)) return;
+    if (!wait_full(C, stage, phase)) return;
 
-    const uint32_t sK = C.base + stage * C.L.stage_bytes + ps * C.L.page_bytes;
-    const uint32_t sV = sK + P.PPS * C.L.page_bytes;
-    const bool is_win = P.window && k == geo.pool_pages;
+    const uint32_t sK = C.base + stage * stage_bytes + ps * page_bytes;
+    const uint32_t sV = sK + v_off;
+    const bool is_win = window && k == geo.pool_pages;
     const int kbase = is_win ? geo.pool_len : k * PAGE;
     const int valid = is_win ? geo.q_len : min(PAGE, geo.pool_len - k * PAGE);
     const int win_start = geo.kv_len - geo.q_len;
-    const bool need_mask = valid < PAGE || (P.a.causal && kbase + PAGE - 1 > win_start);
+    const bool need_mask = valid < PAGE || (causal && kbase + PAGE - 1 > win_start);
 
     // S^T: two accumulators (even / odd k-steps) halve the dependent chain.
     float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
@@ -359,7 +427,7 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
       if (need_mask) {
         const int tok = g4 + 8 * (e >> 1);
         const int r = 2 * c4 + (e & 1);
-        const int lim = P.a.causal ? win_start + r / P.G : geo.kv_len - 1;
+        const int lim = causal ? win_start + r / G : geo.kv_len - 1;
         if (tok >= valid || kbase + tok > lim) v = -INFINITY;
       }
       sc[e] = v;
@@ -382,12 +450,16 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
     }
     pb[0] = movm_trans(M::pack(sc[0], sc[1]));  // -> (row g4, tokens 2c4..2c4+1)
     pb[1] = movm_trans(M::pack(sc[2], sc[3]));  // -> (row g4, tokens 8+2c4..)
+    // The running max rarely moves after the first pages: rescale only when
+    // some row's max changed (alpha != 1) anywhere in the warp.
+    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
-    for (int n = 0; n < D / 16; ++n) {
-      o[n][0] *= alpha[0];
-      o[n][1] *= alpha[1];
-      o[n][2] *= alpha[0];
-      o[n][3] *= alpha[1];
+      for (int n = 0; n < D / 16; ++n) {
+        o[n][0] *= alpha[0];
+        o[n][1] *= alpha[1];
+        o[n][2] *= alpha[0];
+        o[n][3] *= alpha[1];
+      }
     }
     // O^T += V^T P^T, one 16-dim tile per mma
 #pragma unroll
@@ -509,8 +581,11 @@ MF_DEVINL void consume_split(const Ctx& C) {
   float o[DH / 8][4];
   float mrow[2], lrow[2];
 
-  for (int it = 0; it < C.max_len; ++it) {
-    const int stage = it % P.NS;
+  const int NS = P.NS;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int it = 0; it < C.max_len; ++it, stage = (stage + 1 == NS) ? 0 : stage + 1,
+           phase ^= (stage == 0) ? 1u : 0u) {
     if (it >= len) {
       release(C, stage);
       continue;
@@ -547,7 +622,7 @@ MF_DEVINL void consume_split(const Ctx& C) {
       mrow[0] = mrow[1] = -INFINITY;
       lrow[0] = lrow[1] = 0.f;
     }
-    if (!wait_full(C, stage, it)) return;
+    if (!wait_full(C, stage, phase)) return;
 
     const uint32_t sK = C.base + stage * C.L.stage_bytes + ps * C.L.page_bytes;
     const uint32_t sV = sK + P.PPS * C.L.page_bytes;
