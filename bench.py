@@ -234,7 +234,8 @@ def run_ours(args):
     slots_np = (w["tables"][np.arange(B), pos // BLOCK].astype(np.int64) * BLOCK + pos % BLOCK)
     slots = torch.from_numpy(slots_np.astype(np.int32)).to(dev)
     out = torch.empty((B * W, hq, D), device=dev, dtype=torch.bfloat16)
-    gathered = torch.empty((world, B * W, hq, D), device=dev, dtype=torch.bfloat16) if world > 1 else None
+    staging = torch.empty((world * B * W, hq, D), device=dev, dtype=torch.bfloat16) if world > 1 else None
+    full_out = torch.empty((B * W, hq * world, D), device=dev, dtype=torch.bfloat16) if world > 1 else None
     scale = 1.0 / math.sqrt(D)
 
     def step():
@@ -243,7 +244,8 @@ def run_ours(args):
 
     def collective():
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            from memforge_b200.kv_shard import gather_heads
+            gather_heads(out, out=full_out, staging=staging)
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(3, args.warmup)):
@@ -331,8 +333,8 @@ def run_ours(args):
 
 
 # Per-launch DRAM bytes (read + write) of the decode kernel at this workload from
-# one ncu capture (profiles/decode_cfg2.md); None until captured.
-TRAFFIC_BYTES = {}
+# one ncu capture (profiles/decode_cfg2.md: 583.016 MB read + 4.847 MB written).
+TRAFFIC_BYTES = {"cfg2": 587863808}
 
 
 def run_e2e(args, w, dev, kp, vp, hkv, hq, world):
