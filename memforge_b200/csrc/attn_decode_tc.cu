@@ -48,6 +48,8 @@ constexpr size_t SEM_REGION = size_t(1) << 20;
 struct Params {
   AttnParams a;
   int G, HG, NHG, MT, PPS, NS;
+  int rows_cap;   // longest query run (rows = q_len * G) this launch serves
+  int skip_long;  // 1: longer runs belong to another kernel of the same call
   int window;
   float scale_log2;
   float* part;      // partial slots
@@ -91,7 +93,7 @@ MF_DEVINL SeqGeo seq_geo(const Params& P, int i) {
   seq_rows(P.a, i, g.q_start, g.q_len);
   g.kv_len = P.a.kv_lens[i];
   const bool bad = g.q_len < 0 || g.kv_len < g.q_len || (g.q_len > 0 && g.kv_len <= 0) ||
-                   g.q_len * P.G > P.MT * 16 || (P.window && g.q_len > PAGE);
+                   g.q_len * P.G > P.rows_cap || (P.window && g.q_len > PAGE);
   if (bad || g.q_len == 0) {
     g.pool_len = 0;
     g.pool_pages = 0;
@@ -792,7 +794,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   }
   for (int i = tid; i < B; i += blockDim.x) {
     const SeqGeo g = seq_geo(P, i);
-    if (g.q_len > 0 && g.pages == 0) set_err(P.a.err, MF_ERR_LENGTH);
+    const bool other = P.skip_long && g.q_len * P.G > P.rows_cap;
+    if (g.q_len > 0 && g.pages == 0 && !other) set_err(P.a.err, MF_ERR_LENGTH);
     if (g.pages > 0 && (g.pool_len + PAGE - 1) / PAGE > P.a.table_stride)
       set_err(P.a.err, MF_ERR_TABLE);
     prefix[i + 1] = g.pages;
@@ -925,8 +928,10 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
 
 }  // namespace tc
 
-TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool window) {
+TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool window,
+                    bool skip_long) {
   TcPlan pl;
+  pl.skip_long = skip_long;
   auto no = [&](const char* why) {
     pl.ok = false;
     pl.why = why;
@@ -957,6 +962,7 @@ TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool wind
   }
   pl.SW = rows <= 8;
   pl.MT = (rows + 15) / 16;
+  pl.rows_cap = pl.SW ? 8 : pl.MT * 16;
   const int per_head = pl.SW ? 1 : pl.MT * tc::DS;  // consumer warps per kv head
   const int cap = tc::CONSUMER_WARPS / per_head;
   pl.HG = 1;
@@ -1021,6 +1027,8 @@ static int launch_tc_t(const AttnParams& p, const TcPlan& pl, void* ws, cudaStre
   P.MT = pl.MT;
   P.PPS = pl.PPS;
   P.NS = pl.NS;
+  P.rows_cap = pl.rows_cap;
+  P.skip_long = pl.skip_long ? 1 : 0;
   P.window = window ? 1 : 0;
   P.scale_log2 = p.scale * 1.4426950408889634f;
   P.sems = static_cast<int32_t*>(ws);

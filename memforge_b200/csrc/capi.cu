@@ -98,6 +98,33 @@ static int to_params(const mf_attention_args* a, int32_t* err, AttnParams& p) {
   return MF_OK;
 }
 
+// Decode kernel alone when every query run is short (<= 64 rows per kv head);
+// otherwise the tcgen05 prefill kernel for runs of more than 8 rows plus the
+// decode kernel for the rest (each skips the other's sequences on the device,
+// so the split needs no host knowledge of the lengths); the generic kernel
+// for anything neither serves.
+Dispatch plan_dispatch(const AttnParams& p, mf_dtype dtype, int sm_count) {
+  Dispatch d;
+  const bool window = p.wk != nullptr;
+  d.decode = plan_attn_tc(p, dtype, sm_count, window);
+  if (d.decode.ok) {
+    d.mode = Dispatch::DECODE;
+    return d;
+  }
+  const int G = p.hq / p.hkv;
+  if (!window && G <= 8 && prefill_tc_unsupported(p, dtype) == nullptr) {
+    d.short_p = p;
+    d.short_p.max_q_len = 8 / G;
+    d.decode = plan_attn_tc(d.short_p, dtype, sm_count, false, true);
+    if (d.decode.ok && d.decode.SW) {
+      d.mode = Dispatch::MIXED;
+      return d;
+    }
+  }
+  d.mode = Dispatch::GENERIC;
+  return d;
+}
+
 }  // namespace mf
 
 using namespace mf;
@@ -118,8 +145,8 @@ extern "C" int mf_device_info(int device, int* num_sms, int* is_sm100) {
 extern "C" size_t mf_paged_attention_workspace_size(const mf_attention_args* args, int device) {
   AttnParams p{};
   if (to_params(args, nullptr, p) != MF_OK) return 0;
-  const TcPlan pl = plan_attn_tc(p, args->dtype, sm_count_of(device), p.wk != nullptr);
-  return pl.ok ? pl.ws_bytes : 0;
+  const Dispatch d = plan_dispatch(p, args->dtype, sm_count_of(device));
+  return d.mode == Dispatch::GENERIC ? 0 : d.decode.ws_bytes;
 }
 
 extern "C" int mf_paged_attention(const mf_attention_args* args, void* workspace,
@@ -129,14 +156,15 @@ extern "C" int mf_paged_attention(const mf_attention_args* args, void* workspace
   if (rc != MF_OK) return rc;
   if (p.num_seqs == 0 || p.total_q == 0) return MF_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const TcPlan pl = plan_attn_tc(p, args->dtype, current_sm_count(), p.wk != nullptr);
-  if (pl.ok) {
-    if (!workspace || workspace_bytes < pl.ws_bytes)
-      return fail(MF_EWORKSPACE, "paged attention: workspace missing or smaller than "
-                                 "mf_paged_attention_workspace_size()");
-    return launch_attn_tc(p, args->dtype, pl, workspace, s);
-  }
-  return launch_attn_generic(p, args->dtype, s);
+  const Dispatch d = plan_dispatch(p, args->dtype, current_sm_count());
+  if (d.mode == Dispatch::GENERIC) return launch_attn_generic(p, args->dtype, s);
+  if (!workspace || workspace_bytes < d.decode.ws_bytes)
+    return fail(MF_EWORKSPACE, "paged attention: workspace missing or smaller than "
+                               "mf_paged_attention_workspace_size()");
+  if (d.mode == Dispatch::DECODE) return launch_attn_tc(p, args->dtype, d.decode, workspace, s);
+  rc = launch_attn_prefill_tc(p, args->dtype, d.decode.rows_cap, s);
+  if (rc != MF_OK) return rc;
+  return launch_attn_tc(d.short_p, args->dtype, d.decode, workspace, s);
 }
 
 extern "C" int mf_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,

@@ -51,13 +51,30 @@ struct TcPlan {
   bool ok = false;
   const char* why = "";
   bool SW = false;  // swapped-operand decode consumer (<= 8 rows per kv head)
+  bool skip_long = false;
+  int rows_cap = 0;
   int MT = 1, HG = 1, NHG = 1, PPS = 1, NS = 2, ctas = 0;
   size_t smem = 0;
   size_t part_floats = 0;   // floats per partial slot
   size_t ws_bytes = 0;
 };
 
-TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool window);
+TcPlan plan_attn_tc(const AttnParams& p, mf_dtype dtype, int sm_count, bool window,
+                    bool skip_long = false);
+
+// tcgen05 prefill kernel: nullptr when it serves these arguments, else why not.
+const char* prefill_tc_unsupported(const AttnParams& p, mf_dtype dtype);
+// Serves every sequence whose query run has more than rows_cap rows per kv head.
+int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
+                           cudaStream_t stream);
+
+// How one mf_paged_attention call is split across kernels.
+struct Dispatch {
+  enum Mode { DECODE, MIXED, GENERIC } mode = GENERIC;
+  TcPlan decode;      // DECODE / MIXED: the decode kernel's plan
+  AttnParams short_p;  // MIXED: the decode kernel's view (short runs only)
+};
+Dispatch plan_dispatch(const AttnParams& p, mf_dtype dtype, int sm_count);
 int launch_attn_tc(const AttnParams& p, mf_dtype dtype, const TcPlan& plan, void* ws,
                    cudaStream_t stream);
 
