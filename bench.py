@@ -445,13 +445,162 @@ def run_reference(args):
     return res
 
 
+# ------------------------------------------------- other BASELINE configs
+
+def _pool(NB, hkv, D, dev, seed):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    kp = torch.randn((NB, BLOCK, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    vp = torch.randn((NB, BLOCK, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    return kp, vp, g
+
+
+def _time(fn, steps, warmup, dev):
+    import torch
+    for _ in range(max(3, warmup)):
+        fn()
+    torch.cuda.synchronize(dev)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize(dev)
+    return s.elapsed_time(e) / steps
+
+
+def run_cfg3(args):
+    """
+    One pass of BASELINE config 3: 16 prefill chunks (<= 512 tokens over a paged
+    prefix) + 48 decode tokens.  The chunk's K/V are written first (as MemForge's
+    VarlenPackedCacheLayer.update does), then one paged attention call serves
+    every row.  Prefill FLOPs count causally visible pairs only:
+    4 * D * Hq * sum over prefill rows of (position + 1).
+    """
+    import torch
+    from memforge_b200 import _kernels as K
+    from tests import cases
+    dev = torch.device("cuda", 0)
+    meta = cases.config3_meta(0)
+    q_lens, kv_lens = cases.config3_pass(meta, args.chunk_index)
+    B, Hq, Hkv, D, NB = len(q_lens), 32, 8, 128, meta["num_blocks"]
+    kp, vp, g = _pool(NB, Hkv, D, dev, 3)
+    T = int(q_lens.sum())
+    q = torch.randn((T, Hq, D), generator=g, device=dev, dtype=torch.bfloat16)
+    nk = torch.randn((T, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    nv = torch.randn((T, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    tables_np = meta["tables"].clip(min=0)
+    slots, rows_pos = [], []
+    for s_, (ql, kl) in enumerate(zip(q_lens, kv_lens)):
+        for i in range(ql):
+            pos = kl - ql + i
+            rows_pos.append(pos)
+            slots.append(int(tables_np[s_, pos // BLOCK]) * BLOCK + pos % BLOCK)
+    slots = torch.tensor(slots, dtype=torch.int32, device=dev)
+    tables = torch.from_numpy(tables_np).to(dev)
+    cu = torch.zeros(B + 1, dtype=torch.int32)
+    cu[1:] = torch.from_numpy(np.cumsum(q_lens))
+    cu = cu.to(dev)
+    kv = torch.from_numpy(kv_lens).to(dev)
+    scale = 1 / math.sqrt(D)
+    maxq = int(q_lens.max())
+    # prefill-only and decode-only sub-batches, to time each kernel
+    pre = [i for i in range(B) if q_lens[i] > 1]
+    dec = [i for i in range(B) if q_lens[i] == 1]
+
+    def sub(idx):
+        qi = torch.cat([q[int(cu[i]):int(cu[i + 1])] for i in idx])
+        cui = torch.zeros(len(idx) + 1, dtype=torch.int32)
+        cui[1:] = torch.from_numpy(np.cumsum(q_lens[idx]))
+        return (qi, torch.empty_like(qi), tables[idx].contiguous(), kv[idx].contiguous(),
+                cui.to(dev), int(q_lens[idx].max()))
+    P_, D_ = sub(pre), sub(dec)
+
+    def full_step():
+        K.reshape_and_cache(nk, nv, kp, vp, slots)
+        K.paged_attention(q, out, kp, vp, tables, kv, cu_seqlens_q=cu, max_q_len=maxq,
+                          scale=scale)
+
+    def prefill_only():
+        K.paged_attention(P_[0], P_[1], kp, vp, P_[2], P_[3], cu_seqlens_q=P_[4], max_q_len=P_[5],
+                          scale=scale)
+
+    def decode_only():
+        K.paged_attention(D_[0], D_[1], kp, vp, D_[2], D_[3], cu_seqlens_q=D_[4], max_q_len=D_[5],
+                          scale=scale)
+    ms = _time(full_step, args.steps, args.warmup, dev)
+    ms_p = _time(prefill_only, args.steps, args.warmup, dev)
+    ms_d = _time(decode_only, args.steps, args.warmup, dev)
+    K.check_device_errors(dev)
+    flops = 0
+    for i in pre:
+        ql, kl = int(q_lens[i]), int(kv_lens[i])
+        flops += 4 * D * Hq * sum(kl - ql + r + 1 for r in range(ql))
+    dbytes = sum(int(kv_lens[i]) * 2 * Hkv * D * 2 + 2 * Hq * D * 2 + ((int(kv_lens[i]) + 15) // 16) * 4
+                 for i in dec)
+    res = {"metric": "varlen chunked prefill + decode (BASELINE config 3, one pass)",
+           "workload": f"config3 pass {args.chunk_index}", "rows": T, "prefill_rows": int(q_lens[pre].sum()),
+           "ms_per_step": round(ms, 4), "attn_tokens_per_s": round(T / (ms * 1e-3), 1),
+           "prefill": {"ms": round(ms_p, 4), "tflops": round(flops / (ms_p * 1e-3) / 1e12, 2),
+                       "flops": flops},
+           "decode": {"ms": round(ms_d, 4), "GBs": round(dbytes / (ms_d * 1e-3) / 1e9, 1)},
+           "dtype": "bf16", "data": "synthetic (seeded)"}
+    print(json.dumps(res), flush=True)
+
+
+def run_cfg4(args):
+    """
+    speculative verify of a 5-token window per sequence
+    (4 drafts + bonus) against the paged context, the window's K/V read from a
+    side buffer, then the commit of the accepted prefix (accepted ~U[0,4]).
+    """
+    import torch
+    from memforge_b200 import _kernels as K
+    from memforge_b200.speculative import commit_accepted, verify_attention
+    from tests import cases
+    dev = torch.device("cuda", 0)
+    meta = cases.config4_meta(0)
+    B, Hq, Hkv, D, W, NB = 32, 40, 8, 128, meta["window"], meta["num_blocks"]
+    kp, vp, g = _pool(NB, Hkv, D, dev, 4)
+    q = torch.randn((B * W, Hq, D), generator=g, device=dev, dtype=torch.bfloat16)
+    wk = torch.randn((B * W, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    wv = torch.randn((B * W, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    tables = torch.from_numpy(meta["tables"].clip(min=0)).to(dev)
+    ctx = torch.from_numpy(meta["ctx"]).to(dev)
+    kvl = (ctx + W).to(torch.int32)
+    acc = torch.from_numpy(meta["accepted"] + 1).to(dev)
+    out = torch.empty_like(q)
+
+    def verify():
+        verify_attention(q, wk, wv, kp, vp, tables, ctx, out=out, kv_lens=kvl)
+
+    def step():
+        verify()
+        commit_accepted(kp, vp, wk, wv, tables, ctx, acc)
+    ms = _time(step, args.steps, args.warmup, dev)
+    ms_v = _time(verify, args.steps, args.warmup, dev)
+    K.check_device_errors(dev)
+    ctxn = meta["ctx"].astype(np.int64)
+    vbytes = int(ctxn.sum()) * 2 * Hkv * D * 2 + B * W * (Hq * D * 2 * 2 + Hkv * D * 2 * 2) + \
+        int(((ctxn + 15) // 16).sum()) * 4
+    peak, kind = measured_peaks()
+    res = {"metric": "speculative verify attention HBM GB/s (BASELINE config 4)",
+           "ms_per_step": round(ms, 4), "verify_ms": round(ms_v, 4),
+           "verify_GBs": round(vbytes / (ms_v * 1e-3) / 1e9, 1),
+           "verify_frac_of_measured_peak": round(vbytes / (ms_v * 1e-3) / 1e9 / peak, 4),
+           "attn_tokens_per_s": round(B * W / (ms * 1e-3), 1), "dtype": "bf16"}
+    print(json.dumps(res), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2")
+    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2")
+    ap.add_argument("--chunk-index", type=int, default=0)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -459,6 +608,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "cfg3":
+        run_cfg3(args)
+    elif args.workload == "cfg4":
+        run_cfg4(args)
     else:
         run_ours(args)
 
