@@ -169,6 +169,35 @@ MF_API int mf_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h
                     size_t workspace_bytes, int32_t* err_flag, mf_stream_t stream);
 
 /*
+ * mf_paged_decode_noalloc — mf_paged_decode without a caller workspace.
+ *
+ * No counterpart in the reference: MemForge always allocates with torch.  This
+ * entry point is for callers that cannot allocate device memory — a host whose
+ * device memory belongs to another allocator, or a plugin that is handed only
+ * its input and output buffers.  It allocates nothing: split-K scratch comes
+ * from a fixed array of MF_NOALLOC_SCRATCH_BYTES inside the library, which every
+ * GPU that loads the library keeps until the process exits.
+ *   - The first call on a device resolves the array's device address (make
+ *     that first call before any stream capture on that device).
+ *   - Batches whose split-K plan needs more than MF_NOALLOC_SCRATCH_BYTES are
+ *     rejected with MF_EWORKSPACE (use mf_paged_decode with a workspace then).
+ *   - All calls share the array: two calls that can run at the same time on the
+ *     GPU (different streams, or different host threads) race and corrupt each
+ *     other's results.  Calls on one stream are safe.
+ * Arguments and semantics are those of mf_paged_decode.
+ */
+#define MF_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+MF_API int mf_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                   const void* key_flat, const void* value_flat,
+                                   int64_t flat_stride_slot, int64_t flat_stride_head,
+                                   int32_t num_slots, const int32_t* block_tables,
+                                   int32_t table_stride, const int32_t* ctx_lens, int32_t batch,
+                                   int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                   int32_t block_size, float scale, mf_dtype dtype, void* out,
+                                   int32_t* err_flag, mf_stream_t stream);
+
+/*
  * Copy-on-write block copy across all layers: for each pair i, block
  * src[i] -> dst[i] in every layer of both pools (prefix_sharing.copy_block,
  * memforge_ml/runtime/prefix_sharing.py:28-42).  Pools are contiguous

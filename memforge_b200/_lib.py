@@ -43,7 +43,7 @@ ERR_NAMES = {
 EXPORTED = (
     "mf_abi_version", "mf_last_error", "mf_device_info", "mf_reshape_and_cache",
     "mf_paged_attention_workspace_size", "mf_paged_attention", "mf_paged_decode",
-    "mf_copy_blocks",
+    "mf_copy_blocks", "mf_paged_decode_noalloc",
 )
 
 c_i32, c_i64, c_f32, c_vp, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
@@ -96,6 +96,9 @@ def _declare(lib):
         c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_i32, c_vp, c_i32,
         c_i32, c_i32, c_i32, c_i32, c_f32, ctypes.c_int, c_vp, c_vp, c_sz, c_vp, c_vp]
     lib.mf_copy_blocks.argtypes = [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp, c_vp]
+    lib.mf_paged_decode_noalloc.argtypes = [
+        c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_i32, c_vp, c_i32,
+        c_i32, c_i32, c_i32, c_i32, c_f32, ctypes.c_int, c_vp, c_vp, c_vp]
     for name in EXPORTED:
         if name not in ("mf_last_error", "mf_paged_attention_workspace_size"):
             getattr(lib, name).restype = ctypes.c_int

@@ -43,7 +43,7 @@ constexpr int DS = 2;  // consumer warps per (head, m-tile): halves of head_dim 
 constexpr uint64_t WAIT_LIMIT = 2000000000ull;  // 2 s of wall time per wait
 constexpr int MAX_SEQS = 4096;
 constexpr int MAX_WINDOW_SEQS = 1024;
-constexpr size_t SEM_REGION = size_t(1) << 20;
+constexpr size_t SEM_REGION = kSemRegionBytes;
 
 struct Params {
   AttnParams a;

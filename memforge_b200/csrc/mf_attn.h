@@ -44,6 +44,10 @@ MF_DEVINL void seq_rows(const AttnParams& p, int s, int& q_start, int& q_len) {
 
 MF_DEVINL int map_row(const AttnParams& p, int r) { return p.row_map ? p.row_map[r] : r; }
 
+// Bytes at the front of a decode workspace that hold arrival counters (they
+// must be zero when a launch starts; every launch leaves the ones it used zero).
+constexpr size_t kSemRegionBytes = size_t(1) << 20;
+
 // Host launchers.
 int launch_attn_generic(const AttnParams& p, mf_dtype dtype, cudaStream_t stream);
 
