@@ -4,7 +4,8 @@
 //  * Work = the concatenated list of KV pages (16-token blocks) of all
 //    sequences, for each group of HG kv heads.  It is cut into equal
 //    contiguous ranges, one per "virtual CTA" (stream-K), so every SM streams
-//    the same number of bytes whatever the context lengths are.  A range that
+//    the same number of bytes whatever the context lengths are (small batches
+//    use fewer ranges, MIN_PAGES pages at least, to bound the merge fan-in).  A range that
 //    covers a whole sequence writes the output directly; a sequence split
 //    across ranges leaves fp32 partials (running max, sum, unnormalised
 //    accumulator) in the workspace and the last range to finish merges them
@@ -44,6 +45,7 @@ constexpr uint64_t WAIT_LIMIT = 2000000000ull;  // 2 s of wall time per wait
 constexpr int MAX_SEQS = 4096;
 constexpr int MAX_WINDOW_SEQS = 1024;
 constexpr size_t SEM_REGION = kSemRegionBytes;
+constexpr int MIN_PAGES = 4;  // fewest pages a virtual CTA is given
 
 struct Params {
   AttnParams a;
@@ -107,14 +109,31 @@ MF_DEVINL SeqGeo seq_geo(const Params& P, int i) {
   return g;
 }
 
-// Virtual-CTA boundaries: the range of vc is [bound(vc), bound(vc+1)).
-MF_DEVINL int64_t bound(int64_t vc, int64_t total, int64_t NV) { return vc * total / NV; }
+// The virtual page list [0, total) cut over the virtual CTAs: range vc is
+// [bound(vc), bound(vc+1)).  The first `rem` ranges hold base+1 pages, the
+// next nv-rem hold base (>= 1), and virtual CTAs from nv on hold none, so
+// every range below nv is non-empty and a page's owner is closed-form.
+struct Split {
+  int64_t total, nv, base, rem;
+  MF_DEVINL int64_t bound(int64_t vc) const {
+    return vc >= nv ? total : vc * base + (vc < rem ? vc : rem);
+  }
+  MF_DEVINL int owner(int64_t page) const {
+    const int64_t big = (base + 1) * rem;
+    return (int)(page < big ? page / (base + 1) : rem + (page - big) / base);
+  }
+  MF_DEVINL int len(int64_t vc) const { return (int)(bound(vc + 1) - bound(vc)); }
+};
 
-MF_DEVINL int owner(int64_t page, int64_t total, int64_t NV) {
-  int64_t vc = page * NV / total;
-  while (vc + 1 < NV && bound(vc + 1, total, NV) <= page) ++vc;
-  while (vc > 0 && bound(vc, total, NV) > page) --vc;
-  return (int)vc;
+MF_DEVINL Split make_split(int64_t total, int64_t nv_max) {
+  Split s;
+  s.total = total;
+  s.nv = (total + MIN_PAGES - 1) / MIN_PAGES;
+  if (s.nv > nv_max) s.nv = nv_max;
+  if (s.nv < 1) s.nv = 1;
+  s.base = total / s.nv;
+  s.rem = total - s.base * s.nv;
+  return s;
 }
 
 // Sequence index i with prefix[i] <= off < prefix[i+1] (prefix nondecreasing).
@@ -168,7 +187,8 @@ struct Ctx {
   volatile int* abort_flag;
   const int* prefix;
   int B;
-  int64_t T1, TP, NV;
+  int64_t T1;
+  Split S;
   int warp, lane, max_len;
 };
 
@@ -191,128 +211,151 @@ struct PartLayout {
 // Merge every covering range's partial for one (sequence, head, unit) with the
 // log-sum-exp identity and write the output rows [row0, row0+RU) (columns
 // [col0, col0+DU) of the head).  Run by the warp whose arrival completed the
-// set.  Latency-bound, so every load of a pass is independent: lane l first
-// reads (m, l) of (range l / RU, row l % RU) for 32/RU ranges at once, then
-// every lane reads its columns of all rows of those ranges.
-template <typename T, int RU, int DU>
-MF_DEVINL void merge_unit(const Ctx& C, const PartLayout<RU, DU>& PL, int hg, int si, int hl,
+// set.  Latency-bound: each round trip loads RB ranges at once, their (m, l)
+// (lane l: range l / RU, row l % RU) together with their accumulator rows as
+// float4 (lane l: columns 4 (l % (DU/4)) .. +3 of rows i*RPL + l / (DU/4)),
+// and skips rows past the unit's query rows.  HALF: the unit has at most RU/2
+// query rows, so a round trip carries twice the ranges.  The arrival that
+// chose this warp (arrive_last) was an acquire, so no fence is needed here.
+template <typename T, int RU, int DU, bool HALF>
+MF_DEVINL void merge_rows(const Ctx& C, const PartLayout<RU, DU>& PL, int hg, int si, int hl,
                           int unit, int row0, int col0) {
-  constexpr int RPP = 32 / RU;  // ranges per pass
+  constexpr int VPR = DU / 4;                 // float4 per accumulator row
+  constexpr int RPL = 32 / VPR;               // rows one warp-wide float4 load covers
+  constexpr int NR = (HALF ? RU / 2 : RU) / RPL;  // float4 per lane per range
+  constexpr int RB = RU == 8 ? (HALF ? 4 : 2) : (HALF ? 2 : 1);  // ranges per round trip
+  static_assert(RB * RU <= 32 && NR >= 1, "merge tiling");
   const Params& P = C.P;
   const int lane = C.lane;
-  const SeqGeo g = seq_geo(P, si);
+  // Geometry without global loads (the prefix sums are in shared memory).
+  int q_start, q_len;
+  seq_rows(P.a, si, q_start, q_len);
+  const int pages = C.prefix[si + 1] - C.prefix[si];
   const int head = hg * P.HG + hl;
   const int64_t vstart = (int64_t)hg * C.T1 + C.prefix[si];
-  const int vc0 = owner(vstart, C.TP, C.NV);
-  const int vc1 = owner(vstart + g.pages - 1, C.TP, C.NV);
-  __threadfence();
-  float Mrun[RU], acc[RU][DU / 32], Lrun = 0.f;  // Lrun: row lane % RU
+  const int vc0 = C.S.owner(vstart);
+  const int vc1 = C.S.owner(vstart + pages - 1);
+  const int rows = min(RU, q_len * P.G - row0);  // rows of this unit that exist
+  const int lr = lane / VPR, lc = (lane % VPR) * 4;
+  float Mrun[RU], Lrun = 0.f;  // Lrun: row lane % RU
+  float4 acc[NR];
 #pragma unroll
-  for (int r = 0; r < RU; ++r) {
-    Mrun[r] = -INFINITY;
+  for (int r = 0; r < RU; ++r) Mrun[r] = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < DU / 32; ++e) acc[r][e] = 0.f;
-  }
-  int c = vc0;
-  while (c <= vc1) {
-    // Gather up to RPP non-empty ranges.
-    float* slots[RPP];
-    int n = 0;
+  for (int i = 0; i < NR; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = vc0; c <= vc1; c += RB) {
+    const int n = min(RB, vc1 - c + 1);
+    float* slots[RB];
 #pragma unroll
-    for (int j = 0; j < RPP; ++j) slots[j] = nullptr;
-    while (c <= vc1 && n < RPP) {
-      if (bound(c + 1, C.TP, C.NV) > bound(c, C.TP, C.NV)) {
-#pragma unroll
-        for (int j = 0; j < RPP; ++j)
-          if (j == n) slots[j] = PL.slot(c, bound(c, C.TP, C.NV) >= vstart ? 0 : 1);
-        ++n;
-      }
-      ++c;
+    for (int j = 0; j < RB; ++j) {
+      const int cj = j < n ? c + j : c;
+      slots[j] = PL.slot(cj, C.S.bound(cj) >= vstart ? 0 : 1);
     }
-    // Pass 1: (m, l) of (range lane / RU, row lane % RU).
+    // One round trip: (m, l) and accumulator rows of all n ranges.
     const int my_r = lane % RU, my_j = lane / RU;
     float mk = -INFINITY, lk = 0.f;
 #pragma unroll
-    for (int j = 0; j < RPP; ++j)
+    for (int j = 0; j < RB; ++j)
       if (j == my_j && j < n) {
         mk = __ldcg(PL.m(slots[j], unit) + my_r);
         lk = __ldcg(PL.l(slots[j], unit) + my_r);
       }
+    float4 v[RB][NR];
+#pragma unroll
+    for (int j = 0; j < RB; ++j)
+#pragma unroll
+      for (int i = 0; i < NR; ++i)
+        v[j][i] = (j < n && i * RPL < rows)
+                      ? __ldcg(reinterpret_cast<const float4*>(PL.acc(slots[j], unit, i * RPL + lr) + lc))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
     float mx = mk;
 #pragma unroll
     for (int o = RU; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     // New running max of every row, and the factor for what was accumulated so far.
-    float Mr_new[RU], scale_old[RU];
+    float scale_old[RU], mu_mine = 0.f, so_mine = 0.f;
 #pragma unroll
     for (int r = 0; r < RU; ++r) {
-      const float mxr = __shfl_sync(0xffffffffu, mx, r);  // lane r holds row r's pass max
-      Mr_new[r] = fmaxf(Mrun[r], mxr);
-      const float mu = Mr_new[r] == -INFINITY ? 0.f : Mr_new[r];
+      const float mn = fmaxf(Mrun[r], __shfl_sync(0xffffffffu, mx, r));
+      const float mu = mn == -INFINITY ? 0.f : mn;
       scale_old[r] = Mrun[r] == -INFINITY ? 0.f : fast_exp2(Mrun[r] - mu);
+      Mrun[r] = mn;
+      if (r == my_r) {
+        mu_mine = mu;
+        so_mine = scale_old[r];
+      }
     }
-    float w;
-    {
-      float mu_mine = 0.f, so_mine = 0.f;
+    const float w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - mu_mine);
+    float lw = w * lk;
 #pragma unroll
-      for (int r = 0; r < RU; ++r)
-        if (r == my_r) {
-          mu_mine = Mr_new[r] == -INFINITY ? 0.f : Mr_new[r];
-          so_mine = scale_old[r];
+    for (int o = RU; o < 32; o <<= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
+    Lrun = Lrun * so_mine + lw;  // lanes with equal lane % RU agree
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      float so = scale_old[i * RPL];
+#pragma unroll
+      for (int t = 1; t < RPL; ++t)
+        if (lr == t) so = scale_old[i * RPL + t];
+      float4& a = acc[i];
+      a.x *= so;
+      a.y *= so;
+      a.z *= so;
+      a.w *= so;
+#pragma unroll
+      for (int j = 0; j < RB; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j * RU + i * RPL + lr);
+        if (j < n) {
+          a.x += wj * v[j][i].x;
+          a.y += wj * v[j][i].y;
+          a.z += wj * v[j][i].z;
+          a.w += wj * v[j][i].w;
         }
-      w = (mk == -INFINITY) ? 0.f : fast_exp2(mk - mu_mine);
-      float lw = w * lk;
-#pragma unroll
-      for (int o = RU; o < 32; o <<= 1) lw += __shfl_xor_sync(0xffffffffu, lw, o);
-      Lrun = Lrun * so_mine + lw;  // lanes with equal lane % RU agree
-    }
-    // Pass 2: every lane accumulates its columns of every row.
-#pragma unroll
-    for (int r = 0; r < RU; ++r) {
-#pragma unroll
-      for (int e = 0; e < DU / 32; ++e) acc[r][e] *= scale_old[r];
-      Mrun[r] = Mr_new[r];
-    }
-#pragma unroll
-    for (int j = 0; j < RPP; ++j) {
-      if (j >= n) break;
-#pragma unroll
-      for (int r = 0; r < RU; ++r) {
-        const float wj = __shfl_sync(0xffffffffu, w, j * RU + r);
-        const float* pa = PL.acc(slots[j], unit, r);
-#pragma unroll
-        for (int e = 0; e < DU / 32; ++e) acc[r][e] += wj * __ldcg(pa + lane + 32 * e);
       }
     }
   }
   T* obase = static_cast<T*>(P.a.out);
 #pragma unroll
-  for (int r = 0; r < RU; ++r) {
+  for (int i = 0; i < NR; ++i) {
+    const int r = i * RPL + lr;
     const float Lr = __shfl_sync(0xffffffffu, Lrun, r);
+    if (r >= rows) continue;
     const int qi = (row0 + r) / P.G, gg = (row0 + r) % P.G;
-    if (qi >= g.q_len) continue;
     const float inv = Lr > 0.f ? 1.f / Lr : 0.f;
-    T* orow = obase + (int64_t)map_row(P.a, g.q_start + qi) * P.a.o_sr +
-              (int64_t)(head * P.G + gg) * P.a.o_sh + col0;
-#pragma unroll
-    for (int e = 0; e < DU / 32; ++e) orow[lane + 32 * e] = from_f32<T>(acc[r][e] * inv);
+    T* orow = obase + (int64_t)map_row(P.a, q_start + qi) * P.a.o_sr +
+              (int64_t)(head * P.G + gg) * P.a.o_sh + col0 + lc;
+    orow[0] = from_f32<T>(acc[i].x * inv);
+    orow[1] = from_f32<T>(acc[i].y * inv);
+    orow[2] = from_f32<T>(acc[i].z * inv);
+    orow[3] = from_f32<T>(acc[i].w * inv);
   }
 }
 
+// Out of line: the streaming loop keeps its registers; picks the HALF form
+// when the unit has at most RU/2 query rows.
+template <typename T, int RU, int DU>
+__device__ __noinline__ void merge_unit(const Ctx& C, const PartLayout<RU, DU>& PL, int hg,
+                                        int si, int hl, int unit, int row0, int col0) {
+  int q_start, q_len;
+  seq_rows(C.P.a, si, q_start, q_len);
+  if (q_len * C.P.G - row0 <= RU / 2)
+    merge_rows<T, RU, DU, true>(C, PL, hg, si, hl, unit, row0, col0);
+  else
+    merge_rows<T, RU, DU, false>(C, PL, hg, si, hl, unit, row0, col0);
+}
+
 // Arrival bookkeeping after a partial was written: true when this warp's
-// arrival completed the set of ranges covering the sequence.
+// arrival completed the set of ranges covering the sequence.  The warp barrier
+// orders every lane's partial stores before lane 0's acquire-release add, which
+// publishes them (release) and, for the last arrival, makes the other ranges'
+// partials visible to the merge that follows (acquire, then the warp barrier).
 MF_DEVINL bool arrive_last(const Ctx& C, int32_t* sem, int hg, int si, int pages) {
-  __threadfence();
   __syncwarp();
   const int64_t vstart = (int64_t)hg * C.T1 + C.prefix[si];
-  const int vc0 = owner(vstart, C.TP, C.NV);
-  const int vc1 = owner(vstart + pages - 1, C.TP, C.NV);
-  // Ranges covering the sequence: [vc0, vc1] minus empty ones (a virtual CTA
-  // owns no page when there are fewer pages than ranges).
-  int covering = 0;
-  for (int c = vc0; c <= vc1; ++c) covering += bound(c + 1, C.TP, C.NV) > bound(c, C.TP, C.NV);
+  // Ranges covering the sequence: [vc0, vc1], all non-empty.
+  const int covering = C.S.owner(vstart + pages - 1) - C.S.owner(vstart) + 1;
   int old = 0;
-  if (C.lane == 0) old = atomicAdd(sem, 1);
+  if (C.lane == 0) old = atom_add_acq_rel_gpu(sem, 1);
   old = __shfl_sync(0xffffffffu, old, 0);
+  __syncwarp();
   return old == covering - 1;
 }
 
@@ -353,8 +396,8 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
   const int ps = C.warp / units;          // virtual CTA within this CTA
   const int g4 = lane >> 2, c4 = lane & 3;
   const int64_t vc = (int64_t)blockIdx.x * P.PPS + ps;
-  const int64_t lo = bound(vc, C.TP, C.NV);
-  const int len = (int)(bound(vc + 1, C.TP, C.NV) - lo);
+  const int64_t lo = C.S.bound(vc);
+  const int len = C.S.len(vc);
   const T* qbase = static_cast<const T*>(P.a.q);
   T* obase = static_cast<T*>(P.a.out);
   const float sl2 = P.scale_log2;
@@ -516,6 +559,7 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
     first_piece = false;
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
+      if (2 * c4 + j >= geo.q_len * G) continue;  // no such query row
       float* pa = PL.acc(sl, hl, 2 * c4 + j);
 #pragma unroll
       for (int n = 0; n < D / 16; ++n) {
@@ -568,8 +612,8 @@ MF_DEVINL void consume_split(const Ctx& C) {
   const int unit = u;  // == (hl * MT + mt) * DS + dh
   const int g4 = lane >> 2, c4 = lane & 3;
   const int64_t vc = (int64_t)blockIdx.x * P.PPS + ps;
-  const int64_t lo = bound(vc, C.TP, C.NV);
-  const int len = (int)(bound(vc + 1, C.TP, C.NV) - lo);
+  const int64_t lo = C.S.bound(vc);
+  const int len = C.S.len(vc);
   const T* qbase = static_cast<const T*>(P.a.q);
   T* obase = static_cast<T*>(P.a.out);
   const float sl2 = P.scale_log2;
@@ -733,6 +777,7 @@ MF_DEVINL void consume_split(const Ctx& C) {
 #pragma unroll
     for (int h2 = 0; h2 < 2; ++h2) {
       const int rr = g4 + 8 * h2;
+      if (mt * 16 + rr >= geo.q_len * P.G) continue;  // no such query row
       float* pacc = PL.acc(sl, unit, rr);
 #pragma unroll
       for (int n = 0; n < DH / 8; ++n)
@@ -820,15 +865,11 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
   __syncthreads();
 
   const int64_t T1 = prefix[B];
-  const int64_t TP = T1 * P.NHG;
-  const int64_t NV = (int64_t)gridDim.x * P.PPS;
-  if (TP == 0) return;
-  // Longest virtual-CTA range of this CTA: every consumer loops this many stages.
-  int max_len = 0;
-  for (int j = 0; j < P.PPS; ++j) {
-    const int64_t vcj = (int64_t)blockIdx.x * P.PPS + j;
-    max_len = max(max_len, (int)(bound(vcj + 1, TP, NV) - bound(vcj, TP, NV)));
-  }
+  if (T1 == 0) return;
+  const Split S = make_split(T1 * P.NHG, (int64_t)gridDim.x * P.PPS);
+  // Longest virtual-CTA range of this CTA (the first one: lengths do not grow
+  // with vc): every consumer loops this many stages.
+  const int max_len = S.len((int64_t)blockIdx.x * P.PPS);
   if (max_len == 0) return;
 
   if (warp == CONSUMER_WARPS) {
@@ -845,8 +886,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
     // Lane j < PPS feeds virtual CTA j; block ids are loaded two pages ahead.
     const bool feeder = lane < P.PPS;
     const int64_t vc = (int64_t)blockIdx.x * P.PPS + lane;
-    const int64_t lo = feeder ? bound(vc, TP, NV) : 0;
-    const int len = feeder ? (int)(bound(vc + 1, TP, NV) - lo) : 0;
+    const int64_t lo = feeder ? S.bound(vc) : 0;
+    const int len = feeder ? S.len(vc) : 0;
     auto block_of = [&](const Cursor& c) -> int {
       if (P.window && c.k == c.pages - 1) return 0;  // window page: no table entry
       return __ldg(P.a.tables + (int64_t)c.i * P.a.table_stride + c.k);
@@ -873,11 +914,8 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
         __syncwarp();
         if (*abort_flag) break;
       }
-      int n = 0;  // pages this stage carries
-      for (int j = 0; j < P.PPS; ++j) {
-        const int64_t vcj = (int64_t)blockIdx.x * P.PPS + j;
-        if (it < (int)(bound(vcj + 1, TP, NV) - bound(vcj, TP, NV))) ++n;
-      }
+      // Pages this stage carries.
+      const int n = __popc(__ballot_sync(0xffffffffu, feeder && it < len));
       if (lane == 0) mbar_arrive_expect_tx(&full[stage], (uint32_t)n * 2u * L.page_bytes);
       __syncwarp();
       if (feeder && it < len) {
@@ -919,7 +957,7 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
 
   // ============================================================== consumers
   if (warp >= active_warps) return;
-  Ctx C{P, L, base, full, empty, abort_flag, prefix, B, T1, TP, NV, warp, lane, max_len};
+  Ctx C{P, L, base, full, empty, abort_flag, prefix, B, T1, S, warp, lane, max_len};
   if constexpr (SW)
     consume_swapped<T, D>(C);
   else
