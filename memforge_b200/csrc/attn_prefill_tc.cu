@@ -1,23 +1,34 @@
 // Paged chunked-prefill attention on the sm_100a tensor cores (tcgen05 + TMEM).
 //
-// One CTA computes one 128-row query tile of one sequence for one kv head.
-// The 128 rows are (query position, query head of the GQA group) pairs, so
-// each K/V tile is loaded once for every query head sharing the kv head.
+// Persistent: one CTA per SM walks a list of work items, each one 128-row
+// query tile of one sequence for one kv head.  The 128 rows are (query
+// position, query head of the GQA group) pairs, so each K/V tile is loaded once
+// for every query head sharing the kv head.
 //
-//   warps 0-3  softmax / correction / epilogue: thread t owns TMEM lane t (row t)
-//   warp 4     TMA producer: Q once, then per 128-key tile 8 pages x 2 halves of
-//              K and of V (4-D tiled loads from the pool, 128-byte swizzled)
-//   warp 5     MMA issuer (one thread): S = Q K^T into TMEM (two S buffers), and
-//              O += P V with P read back from TMEM as the A operand
+//   warps 0..4*WPQ-1  softmax and epilogue: warp w reads TMEM lanes 32 (w % 4) ..
+//              (tile rows) and columns [CW (w / 4), CW (w / 4 + 1)) of S, P and O;
+//              the WPQ warps of one lane quarter combine their partial row maxima
+//              (and, at the end, row sums) through shared memory
+//   next 2     TMA producers: Q (two buffers) and K, and V; per 128-key tile
+//              8 pages x 2 halves (4-D tiled loads from the pool, 128-byte
+//              swizzled) into two-stage K and V rings
+//   last warp  MMA issuer (one thread): S = Q K^T into one of two TMEM S buffers,
+//              O += P V with P read from one of two TMEM P buffers
 //
-// The online softmax keeps a per-row reference max and only rescales O (a TMEM
-// read-modify-write) when a tile's max exceeds it by more than 2^8, so the
-// exponentials stay <= 256 and the correction is rare after the first tiles.
-// Masking: key k is visible to row r iff k < kv_len and k <= kv_len - q_len +
-// position(r) (causal) — the varlen rule of memforge_ml/kernels/
-// varlen_attention.py:193-201.  Pages past the block table load as zeros
-// (out-of-range TMA coordinates) and unwritten slots of the last page are
-// zeroed in shared memory before the P V product.
+// TMEM (512 columns): S_a S_b (128 fp32 each), P_a P_b (64 columns of packed
+// 16-bit pairs each), O (128 fp32).  P does not alias S, so an S buffer is free
+// again as soon as the softmax warps have loaded it, and the MMA issue order
+// S_0 S_1 P_0V_0 S_2 P_1V_1 S_3 ... (across work items too) keeps the next S
+// and the previous P V queued on the tensor pipe while a tile's softmax runs.
+//
+// The online softmax keeps a per-row reference max (log2 units) and only
+// rescales O (a TMEM read-modify-write) when a tile's max exceeds it by more
+// than 2^8, so the exponentials stay <= 256 and the correction is rare after the
+// first tiles.  Masking: key k is visible to row r iff k < kv_len and k <=
+// kv_len - q_len + position(r) (causal) — the varlen rule of
+// memforge_ml/kernels/varlen_attention.py:193-201.  Pages past the block table
+// load as zeros (out-of-range TMA coordinates) and unwritten slots of the last
+// page are zeroed in shared memory before the P V product.
 //
 // Every mbarrier wait is bounded; on expiry the CTA raises MF_ERR_TIMEOUT, drains
 // its TMA loads and MMAs, frees its TMEM and returns.
@@ -27,50 +38,93 @@
 namespace mf {
 namespace pf {
 
-constexpr int THREADS = 192;
 constexpr int BM = 128;
 constexpr int BN = 128;
+constexpr int WPQ = 1;                  // softmax warps per TMEM lane quarter
+constexpr int SM_WARPS = 4 * WPQ;       // softmax warps
+constexpr int CW = BN / WPQ;            // score columns per softmax warp
+constexpr int TMA_WARP = SM_WARPS, V_WARP = SM_WARPS + 1, MMA_WARP = SM_WARPS + 2;
+constexpr int THREADS = (SM_WARPS + 3) * 32;
+// One exponential in POLY_EVERY runs on the FMA pipe (exp2_fma), the rest on
+// the SFU; 0 keeps them all on the SFU.
+constexpr int POLY_EVERY = 0;
+static_assert(CW == 32 || CW == 64 || CW == 128, "softmax column split");
 constexpr int D = 128;
 constexpr int PAGE = 16;
-constexpr int STAGES = 2;
+constexpr int KS = 2;  // K and V ring stages
+constexpr int MAX_SEQS = 4096;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint64_t WAIT_LIMIT = 2000000000ull;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 constexpr uint32_t TILE_BYTES = BN * D * 2;   // 32 KB: [half][128 rows][128 B]
 constexpr uint32_t HALF_BYTES = BN * 128;     // 16 KB
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + TILE_BYTES;
-constexpr uint32_t OFF_V = OFF_K + STAGES * TILE_BYTES;
-constexpr uint32_t OFF_BAR = OFF_V + STAGES * TILE_BYTES;
-// barriers: q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2],
-// s_free[2], p_full[2], o_done, mma_idle
-constexpr int NBAR = 1 + 4 * STAGES + 6 + 2;
-constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr uint32_t SMEM_BYTES = OFF_MISC + 64;
+constexpr uint32_t OFF_Q = 0;                 // two Q buffers
+constexpr uint32_t OFF_K = OFF_Q + 2 * TILE_BYTES;
+constexpr uint32_t OFF_V = OFF_K + KS * TILE_BYTES;
+constexpr uint32_t OFF_BAR = OFF_V + KS * TILE_BYTES;
+
+// mbarrier indices
+constexpr int B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = B_KFULL + KS,
+              B_VFULL = B_KEMPTY + KS, B_VEMPTY = B_VFULL + KS, B_SFULL = B_VEMPTY + KS,
+              B_SFREE = B_SFULL + 2, B_PFULL = B_SFREE + 2, B_PVDONE = B_PFULL + 2,
+              B_OFULL = B_PVDONE + 2, B_OFREE = B_OFULL + 1, B_IDLE = B_OFREE + 1,
+              B_XCH = B_IDLE + 1, NBAR = B_XCH + 4;
+constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
+// Row-statistic exchange between the softmax warps of a lane quarter: two
+// buffers of [WPQ][BM] floats.
+constexpr uint32_t OFF_XCH = OFF_MISC + 16;
+constexpr uint32_t OFF_PREFIX = OFF_XCH + 2 * WPQ * BM * 4;  // int[num_seqs + 1]
+
+// TMEM column offsets
+constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;
+
+__host__ __device__ constexpr uint32_t smem_bytes(int num_seqs) {
+  return OFF_PREFIX + (uint32_t)(num_seqs + 1) * 4u;
+}
 
 struct Params {
   AttnParams a;
   int G;
   int rows_cap;      // sequences with q_len * G <= rows_cap belong to the decode kernel
-  int q_tiles;       // grid.x = num_seqs * q_tiles
   float scale_log2;
   uint32_t in_fmt;   // 0 = f16, 1 = bf16
 };
 
-struct Bars {
-  uint64_t* base;
-  MF_DEVINL uint64_t* q_full() const { return base; }
-  MF_DEVINL uint64_t* k_full(int s) const { return base + 1 + s; }
-  MF_DEVINL uint64_t* k_empty(int s) const { return base + 1 + STAGES + s; }
-  MF_DEVINL uint64_t* v_full(int s) const { return base + 1 + 2 * STAGES + s; }
-  MF_DEVINL uint64_t* v_empty(int s) const { return base + 1 + 3 * STAGES + s; }
-  MF_DEVINL uint64_t* s_full(int b) const { return base + 1 + 4 * STAGES + b; }
-  MF_DEVINL uint64_t* s_free(int b) const { return base + 3 + 4 * STAGES + b; }
-  MF_DEVINL uint64_t* p_full(int b) const { return base + 5 + 4 * STAGES + b; }
-  MF_DEVINL uint64_t* o_done() const { return base + 7 + 4 * STAGES; }
-  MF_DEVINL uint64_t* mma_idle() const { return base + 8 + 4 * STAGES; }
+// Geometry of one work item (identical in every role).
+struct Item {
+  int s, h, q_start, q_len, kv_len, win_start, pos0, nt;
 };
+
+MF_DEVINL int find_tile_seq(const int* prefix, int B, int t) {
+  int lo = 0, hi = B;  // prefix[lo] <= t < prefix[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= t) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// Items are ordered so that the tiles with the most keys (the last tiles of
+// each sequence) come first.
+MF_DEVINL Item item_at(const Params& P, const int* prefix, int B, int it) {
+  Item I;
+  const int hkv = P.a.hkv;
+  const int T = prefix[B];
+  const int t = T - 1 - it / hkv;
+  I.h = it % hkv;
+  I.s = find_tile_seq(prefix, B, t);
+  const int qt = t - prefix[I.s];
+  seq_rows(P.a, I.s, I.q_start, I.q_len);
+  I.kv_len = __ldg(P.a.kv_lens + I.s);
+  I.win_start = I.kv_len - I.q_len;
+  const int ppt = BM / P.G;
+  I.pos0 = qt * ppt;
+  const int pos_last = min(I.q_len - 1, I.pos0 + ppt - 1);
+  const int key_end = I.win_start + pos_last + 1;  // keys this tile can see
+  I.nt = (key_end + BN - 1) / BN;
+  return I;
+}
 
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
@@ -80,55 +134,54 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw_base);
-  Bars bars{reinterpret_cast<uint64_t*>(gbase + OFF_BAR)};
+  uint64_t* bar = reinterpret_cast<uint64_t*>(gbase + OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_MISC + 4);
+  int* prefix = reinterpret_cast<int*>(gbase + OFF_PREFIX);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int s = blockIdx.x / P.q_tiles;
-  const int qt = blockIdx.x % P.q_tiles;
-  const int h = blockIdx.y;  // kv head
+  const int B = P.a.num_seqs;
   const int G = P.G;
-  const int ppt = BM / G;    // query positions per tile
-
-  int q_start, q_len;
-  seq_rows(P.a, s, q_start, q_len);
-  const int kv_len = P.a.kv_lens[s];
-  // Whole-CTA early exits (uniform): short sequences belong to the decode kernel.
-  if (q_len <= 0 || q_len * G <= P.rows_cap || qt * ppt >= q_len) return;
-  if (kv_len < q_len) {
-    if (tid == 0 && qt == 0 && h == 0) set_err(P.a.err, MF_ERR_LENGTH);
-    return;
-  }
-  const int win_start = kv_len - q_len;
-  const int pos0 = qt * ppt;
-  const int pos_last = min(q_len - 1, pos0 + ppt - 1);
-  const int key_end = win_start + pos_last + 1;            // keys this tile can see
-  const int ntiles = (key_end + BN - 1) / BN;
-  const int pool_pages = (kv_len + PAGE - 1) / PAGE;
-  if (pool_pages > P.a.table_stride) {
-    if (tid == 0) set_err(P.a.err, MF_ERR_TABLE);
-    return;
-  }
 
   // ------------------------------------------------------------- set-up
   if (tid == 0) {
-    mbar_init(bars.q_full(), 1);
-    for (int st = 0; st < STAGES; ++st) {
-      mbar_init(bars.k_full(st), 1);
-      mbar_init(bars.k_empty(st), 1);
-      mbar_init(bars.v_full(st), 1);
-      mbar_init(bars.v_empty(st), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar[B_QFULL + i], 1);
+      mbar_init(&bar[B_QEMPTY + i], 1);
+      mbar_init(&bar[B_SFULL + i], 1);
+      mbar_init(&bar[B_SFREE + i], SM_WARPS);
+      mbar_init(&bar[B_PFULL + i], SM_WARPS);
+      mbar_init(&bar[B_PVDONE + i], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bars.s_full(b), 1);
-      mbar_init(bars.s_free(b), 1);
-      mbar_init(bars.p_full(b), 4);
+    for (int st = 0; st < KS; ++st) {
+      mbar_init(&bar[B_KFULL + st], 1);
+      mbar_init(&bar[B_KEMPTY + st], 1);
+      mbar_init(&bar[B_VFULL + st], 1);
+      mbar_init(&bar[B_VEMPTY + st], 1);
     }
-    mbar_init(bars.o_done(), 1);
-    mbar_init(bars.mma_idle(), 1);
+    mbar_init(&bar[B_OFULL], 1);
+    mbar_init(&bar[B_OFREE], SM_WARPS);
+    mbar_init(&bar[B_IDLE], 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&bar[B_XCH + q], WPQ);
     *abort_flag = 0;
     fence_barrier_init();
+  }
+  // Query tiles per sequence: only runs longer than rows_cap rows are served here.
+  for (int i = tid; i < B; i += THREADS) {
+    int qs, ql;
+    seq_rows(P.a, i, qs, ql);
+    int tiles = 0;
+    if (ql > 0 && ql * G > P.rows_cap) {
+      const int kvl = P.a.kv_lens[i];
+      if (kvl < ql) {
+        set_err(P.a.err, MF_ERR_LENGTH);
+      } else if ((kvl + PAGE - 1) / PAGE > P.a.table_stride) {
+        set_err(P.a.err, MF_ERR_TABLE);
+      } else {
+        tiles = (ql * G + BM - 1) / BM;
+      }
+    }
+    prefix[i + 1] = tiles;
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -136,237 +189,389 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
   }
   tc_fence_before();
   __syncthreads();
+  if (warp == 0) {
+    int run = 0;
+    if (lane == 0) prefix[0] = 0;
+    for (int c0 = 0; c0 < B; c0 += 32) {
+      const int i = c0 + lane;
+      int v = (i < B) ? prefix[i + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      if (i < B) prefix[i + 1] = run + v;
+      run += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};  // S / P buffers (columns)
-  const uint32_t tO = tmem + 256;             // O accumulator (128 fp32 columns)
+  const int items = prefix[B] * P.a.hkv;
 
-  if (warp == 4) {
-    // ======================================================== TMA producer
+  if (warp == TMA_WARP || warp == V_WARP) {
+    // ======================================================= TMA producers
+    // One warp loads Q and K, another V: the K ring frees at S completion and
+    // the V ring only at P V completion, so K loads never queue behind V.
     if (lane == 0) {
+      const bool is_v = warp == V_WARP;
       const uint64_t pol_once = l2_evict_first_policy();
       const uint64_t pol_keep = l2_evict_last_policy();
-      prefetch_tmap(&tmq);
-      prefetch_tmap(&tmk);
-      prefetch_tmap(&tmv);
-      mbar_arrive_expect_tx(bars.q_full(), TILE_BYTES);
-      for (int half = 0; half < 2; ++half)
-        tma_load_4d(gbase + OFF_Q + half * HALF_BYTES, &tmq, bars.q_full(), 0, h * G, half,
-                    q_start + pos0, pol_once);
+      if (!is_v) {
+        prefetch_tmap(&tmq);
+        prefetch_tmap(&tmk);
+      } else {
+        prefetch_tmap(&tmv);
+      }
+      const CUtensorMap* tmap = is_v ? &tmv : &tmk;
+      const uint32_t ring = is_v ? OFF_V : OFF_K;
+      uint64_t* fullb = &bar[is_v ? B_VFULL : B_KFULL];
+      uint64_t* emptyb = &bar[is_v ? B_VEMPTY : B_KEMPTY];
       const int nb = P.a.num_blocks;
-      const int32_t* table = P.a.tables + (int64_t)s * P.a.table_stride;
-      int armed = 0, armed_k = 0;  // tiles whose V (K) loads were issued
-      for (int j = 0; j < ntiles && !*abort_flag; ++j) {
-        const int st = j % STAGES;
-        const uint32_t ph = ((j / STAGES) - 1) & 1;
-        for (int kv = 0; kv < 2; ++kv) {
-          uint64_t* empty = kv ? bars.v_empty(st) : bars.k_empty(st);
-          uint64_t* full = kv ? bars.v_full(st) : bars.k_full(st);
-          if (j >= STAGES && !mbar_wait_bounded(empty, ph, WAIT_LIMIT)) {
+      uint32_t g = 0;      // tiles started (all items)
+      uint32_t armed = 0;  // tiles whose loads were issued
+      int ic = 0;          // items whose Q load was issued (lane 0)
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const Item I = item_at(P, prefix, B, it);
+        if (!is_v) {
+          const int qb = ic & 1;
+          if (ic >= 2 &&
+              !mbar_wait_bounded(&bar[B_QEMPTY + qb], ((ic >> 1) - 1) & 1, WAIT_LIMIT)) {
             set_err(P.a.err, MF_ERR_TIMEOUT);
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(full, TILE_BYTES);
-          uint8_t* dst = gbase + (kv ? OFF_V : OFF_K) + st * TILE_BYTES;
+          mbar_arrive_expect_tx(&bar[B_QFULL + qb], TILE_BYTES);
+          for (int half = 0; half < 2; ++half)
+            tma_load_4d(gbase + OFF_Q + qb * TILE_BYTES + half * HALF_BYTES, &tmq,
+                        &bar[B_QFULL + qb], 0, I.h * G, half, I.q_start + I.pos0, pol_once);
+          ++ic;
+        }
+        const int pool_pages = (I.kv_len + PAGE - 1) / PAGE;
+        const int32_t* table = P.a.tables + (int64_t)I.s * P.a.table_stride;
+        // Block ids of a tile's 8 pages, loaded one tile ahead (independent
+        // loads, consumed a tile later) so the table reads stay off the TMA
+        // issue path.  Out-of-table pages use an out-of-range coordinate: TMA
+        // fills zeros.
+        auto load_ids = [&](int j, int* ids) {
+#pragma unroll
           for (int pg = 0; pg < BN / PAGE; ++pg) {
             const int L = j * (BN / PAGE) + pg;
-            int tok = nb * PAGE;  // out of range: TMA fills zeros
+            ids[pg] = L < pool_pages ? __ldg(table + L) : -1;
+          }
+        };
+        int nxt[BN / PAGE];
+        load_ids(0, nxt);
+        for (int j = 0; j < I.nt; ++j, ++g) {
+          int tok[BN / PAGE];
+#pragma unroll
+          for (int pg = 0; pg < BN / PAGE; ++pg) {
+            const int L = j * (BN / PAGE) + pg;
+            tok[pg] = nb * PAGE;
             if (L < pool_pages) {
-              const int blk = __ldg(table + L);
-              if (blk >= 0 && blk < nb) tok = blk * PAGE;
+              if (nxt[pg] >= 0 && nxt[pg] < nb) tok[pg] = nxt[pg] * PAGE;
               else set_err(P.a.err, MF_ERR_BLOCK_ID);
             }
-            for (int half = 0; half < 2; ++half)
-              tma_load_4d(dst + half * HALF_BYTES + pg * PAGE * 128, kv ? &tmv : &tmk, full, 0,
-                          tok, half, h, pol_keep);
           }
-          if (kv == 0) armed_k = j + 1;
-          else armed = j + 1;
+          if (j + 1 < I.nt) load_ids(j + 1, nxt);
+          const int st = g % KS;
+          if (g >= KS && !mbar_wait_bounded(&emptyb[st], ((g / KS) - 1) & 1, WAIT_LIMIT)) {
+            set_err(P.a.err, MF_ERR_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          mbar_arrive_expect_tx(&fullb[st], TILE_BYTES);
+          armed = g + 1;
+          uint8_t* dst = gbase + ring + st * TILE_BYTES;
+#pragma unroll
+          for (int pg = 0; pg < BN / PAGE; ++pg)
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+              tma_load_4d(dst + half * HALF_BYTES + pg * PAGE * 128, tmap, &fullb[st], 0,
+                          tok[pg], half, I.h, pol_keep);
         }
-        if (*abort_flag) break;
       }
-      // Drain every armed load before the CTA can exit.
-      for (int j = max(0, armed_k - STAGES); j < armed_k; ++j)
-        if (!mbar_wait_bounded(bars.k_full(j % STAGES), (j / STAGES) & 1, WAIT_LIMIT))
+      // Drain every armed load before the CTA can exit (the ring holds the
+      // last KS tiles and, for lane 0, the last two Q tiles in flight at most).
+      for (uint32_t k = armed > (uint32_t)KS ? armed - KS : 0u; k < armed; ++k)
+        if (!mbar_wait_bounded(&fullb[k % KS], (k / KS) & 1, WAIT_LIMIT))
           set_err(P.a.err, MF_ERR_TIMEOUT);
-      for (int j = max(0, armed - STAGES); j < armed; ++j)
-        if (!mbar_wait_bounded(bars.v_full(j % STAGES), (j / STAGES) & 1, WAIT_LIMIT))
-          set_err(P.a.err, MF_ERR_TIMEOUT);
-      mbar_wait_bounded(bars.q_full(), 0, WAIT_LIMIT);
+      if (!is_v)
+        for (int i = ic > 2 ? ic - 2 : 0; i < ic; ++i)
+          if (!mbar_wait_bounded(&bar[B_QFULL + (i & 1)], (i >> 1) & 1, WAIT_LIMIT))
+            set_err(P.a.err, MF_ERR_TIMEOUT);
     }
-  } else if (warp == 5) {
+  } else if (warp == MMA_WARP) {
     // ========================================================= MMA issuer
     if (lane == 0) {
       const uint32_t idesc_s = idesc_f16(BM, BN, P.in_fmt, false);
       const uint32_t idesc_o = idesc_f16(BM, D, P.in_fmt, true);
-      bool ok = mbar_wait_bounded(bars.q_full(), 0, WAIT_LIMIT);
-      tc_fence_after();
-      for (int j = 0; ok && j < ntiles + 1; ++j) {
-        // S_j = Q K_j^T  (issued one tile ahead of P_{j-1} V_{j-1})
-        if (j < ntiles) {
-          const int st = j % STAGES, b = j & 1;
-          if (j >= 2) ok = ok && mbar_wait_bounded(bars.s_free(b), ((j >> 1) - 1) & 1, WAIT_LIMIT);
-          ok = ok && mbar_wait_bounded(bars.k_full(st), (j / STAGES) & 1, WAIT_LIMIT);
+      const uint32_t tO = tmem + COL_O;
+      bool ok = true;
+      // The P V product of one tile is issued after the S of the next tile.
+      bool pend = false;
+      uint32_t pg_ = 0;  // pending tile (global index)
+      int p_first = 0, p_last = 0, p_item = 0;
+      auto issue_pv = [&]() {
+        const int pb = pg_ & 1, st = pg_ % KS;
+        ok = ok && mbar_wait_bounded(&bar[B_PFULL + pb], (pg_ >> 1) & 1, WAIT_LIMIT);
+        ok = ok && mbar_wait_bounded(&bar[B_VFULL + st], (pg_ / KS) & 1, WAIT_LIMIT);
+        // The first P V of an item overwrites O: the previous epilogue must have read it.
+        if (p_first && p_item > 0)
+          ok = ok && mbar_wait_bounded(&bar[B_OFREE], (p_item - 1) & 1, WAIT_LIMIT);
+        if (!ok || *abort_flag) return;
+        tc_fence_after();
+        const uint32_t vb = base + OFF_V + st * TILE_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < BN / 16; ++ks)
+          // P columns ks*8 .. (16 keys packed 2 per column); V rows ks*16 ..
+          umma_ts(tO, tmem + COL_P + pb * 64 + ks * 8,
+                  sdesc_sw128(vb + ks * 16 * 128, HALF_BYTES, 1024), idesc_o,
+                  (p_first && ks == 0) ? 0u : 1u);
+        umma_commit(&bar[B_VEMPTY + st]);
+        umma_commit(&bar[B_PVDONE + pb]);
+        if (p_last) umma_commit(&bar[B_OFULL]);
+        pend = false;
+      };
+      uint32_t g = 0;
+      int ic = 0;
+      for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++ic) {
+        const Item I = item_at(P, prefix, B, it);
+        const int qb = ic & 1;
+        ok = mbar_wait_bounded(&bar[B_QFULL + qb], (ic >> 1) & 1, WAIT_LIMIT);
+        const uint32_t qbase = base + OFF_Q + qb * TILE_BYTES;
+        for (int j = 0; ok && j < I.nt; ++j, ++g) {
+          const int sb = g & 1, st = g % KS;
+          if (g >= 2) ok = ok && mbar_wait_bounded(&bar[B_SFREE + sb], ((g >> 1) - 1) & 1, WAIT_LIMIT);
+          ok = ok && mbar_wait_bounded(&bar[B_KFULL + st], (g / KS) & 1, WAIT_LIMIT);
           if (!ok || *abort_flag) break;
           tc_fence_after();
-          const uint32_t qb = base + OFF_Q, kb = base + OFF_K + st * TILE_BYTES;
+          const uint32_t kb = base + OFF_K + st * TILE_BYTES;
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t off = (ks >> 2) * HALF_BYTES + (ks & 3) * 32;
-            umma_ss(tS[b], sdesc_sw128(qb + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024),
-                    idesc_s, ks > 0);
+            umma_ss(tmem + COL_S + sb * 128, sdesc_sw128(qbase + off, 16, 1024),
+                    sdesc_sw128(kb + off, 16, 1024), idesc_s, ks > 0);
           }
-          umma_commit(bars.k_empty(st));
-          umma_commit(bars.s_full(b));
-        }
-        // O += P_{j-1} V_{j-1}
-        if (j >= 1) {
-          const int jj = j - 1, st = jj % STAGES, b = jj & 1;
-          ok = ok && mbar_wait_bounded(bars.p_full(b), (jj >> 1) & 1, WAIT_LIMIT);
-          ok = ok && mbar_wait_bounded(bars.v_full(st), (jj / STAGES) & 1, WAIT_LIMIT);
+          umma_commit(&bar[B_KEMPTY + st]);
+          umma_commit(&bar[B_SFULL + sb]);
+          if (j == I.nt - 1) umma_commit(&bar[B_QEMPTY + qb]);
+          if (pend) issue_pv();
           if (!ok || *abort_flag) break;
-          tc_fence_after();
-          const uint32_t vb = base + OFF_V + st * TILE_BYTES;
-#pragma unroll
-          for (int ks = 0; ks < BN / 16; ++ks) {
-            // P columns ks*8 .. (16 bf16 keys packed 2 per column); V rows ks*16 ..
-            umma_ts(tO, tS[b] + ks * 8, sdesc_sw128(vb + ks * 16 * 128, HALF_BYTES, 1024),
-                    idesc_o, (jj > 0 || ks > 0) ? 1u : 0u);
-          }
-          umma_commit(bars.v_empty(st));
-          umma_commit(bars.s_free(b));
-          umma_commit(bars.o_done());
+          pend = true;
+          pg_ = g;
+          p_first = j == 0;
+          p_last = j == I.nt - 1;
+          p_item = ic;
         }
       }
+      if (ok && pend && !*abort_flag) issue_pv();
       if (!ok) {
         set_err(P.a.err, MF_ERR_TIMEOUT);
         *abort_flag = 1;
       }
       // Every MMA issued above has completed before TMEM can be freed.
-      umma_commit(bars.mma_idle());
-      if (!mbar_wait_bounded(bars.mma_idle(), 0, WAIT_LIMIT)) set_err(P.a.err, MF_ERR_TIMEOUT);
+      umma_commit(&bar[B_IDLE]);
+      if (!mbar_wait_bounded(&bar[B_IDLE], 0, WAIT_LIMIT)) set_err(P.a.err, MF_ERR_TIMEOUT);
     }
   } else {
-    // ================================================ softmax (warps 0-3)
-    const int row = tid;  // TMEM lane == tile row
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const int pos = pos0 + row / G;  // query position of this row within the sequence
-    const int g = row % G;
-    const int limit = win_start + pos;  // last visible key (causal)
+    // ====================================== softmax (warps 0 .. SM_WARPS-1)
+    const int quarter = warp & 3, cs = warp >> 2;
+    const int row = quarter * 32 + lane;  // TMEM lane == tile row
+    const int col0 = cs * CW;             // this warp's columns of S / O
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tO = tmem + COL_O + lane_off + col0;
+    float* xch = reinterpret_cast<float*>(gbase + OFF_XCH);
     const float sl2 = P.scale_log2;
-    float m_ref = -INFINITY, l_sum = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1;
-      if (!mbar_wait_bounded(bars.s_full(b), (j >> 1) & 1, WAIT_LIMIT)) {
-        ok = false;
+    uint32_t xc = 0;  // exchanges done by this warp
+    // Combine one per-row value over the WPQ warps of this lane quarter (max
+    // or sum); false (on every lane) when the bounded wait gave up.
+    auto exchange = [&](float v, bool is_max, float& out) -> bool {
+      if (WPQ == 1) {
+        out = v;
+        return true;
       }
-      // Warp-uniform decision: tcgen05.ld/st below are warp-collective.
-      if (__any_sync(0xffffffffu, !ok || *abort_flag != 0)) {
+      float* buf = xch + (xc & 1) * WPQ * BM;
+      buf[cs * BM + row] = v;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_XCH + quarter]);
+      const bool fine = mbar_wait_bounded(&bar[B_XCH + quarter], xc & 1, WAIT_LIMIT);
+      ++xc;
+      if (__any_sync(0xffffffffu, !fine)) return false;
+      float r = buf[row];
+#pragma unroll
+      for (int k = 1; k < WPQ; ++k) r = is_max ? fmaxf(r, buf[k * BM + row]) : r + buf[k * BM + row];
+      out = r;
+      return true;
+    };
+    uint32_t g = 0;
+    int ic = 0;
+    for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++ic) {
+      const Item I = item_at(P, prefix, B, it);
+      const int pos = I.pos0 + row / G;  // query position of this row within the sequence
+      const int gg = row % G;
+      const int limit = min(I.win_start + pos, I.kv_len - 1);  // last visible key
+      float m_ref = -INFINITY, l_sum = 0.f;
+      for (int j = 0; j < I.nt; ++j, ++g) {
+        const int sb = g & 1, pb = g & 1;
+        if (!mbar_wait_bounded(&bar[B_SFULL + sb], (g >> 1) & 1, WAIT_LIMIT)) ok = false;
+        // Warp-uniform decision: tcgen05.ld/st below are warp-collective.
+        if (__any_sync(0xffffffffu, !ok || *abort_flag != 0)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float sv[CW];
+#pragma unroll
+        for (int c = 0; c < CW / 32; ++c)
+          tmem_ld32(tmem + COL_S + sb * 128 + lane_off + col0 + c * 32,
+                    reinterpret_cast<uint32_t*>(sv + c * 32));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_SFREE + sb]);  // S buffer may be overwritten
+
+        // Row max of the raw scores over the visible columns (col0 + c <= limit).
+        const int lim = limit - j * BN - col0;
+        if (__any_sync(0xffffffffu, lim < CW - 1)) {
+#pragma unroll
+          for (int c = 0; c < CW; ++c)
+            if (c > lim) sv[c] = -INFINITY;
+        }
+        float mx[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = sv[e];
+#pragma unroll
+        for (int c = 8; c < CW; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+        float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        if (!exchange(mraw, true, mraw)) {
+          ok = false;
+          break;
+        }
+        // Lazy rescale: a row keeps its reference max unless this tile exceeds
+        // it by more than 2^8 (the same decision in every warp of the row).  The
+        // O correction is a warp-collective TMEM read-modify-write, done when
+        // any row of the warp needs it (the other rows multiply by 1).
+        const float tmax = mraw * sl2;
+        float f = 1.f;
+        if (mraw != -INFINITY && (m_ref == -INFINITY || tmax > m_ref + RESCALE_THRESHOLD)) {
+          if (m_ref != -INFINITY) f = fast_exp2(m_ref - tmax);
+          m_ref = tmax;
+        }
+        l_sum *= f;
+        if (j > 0 && __any_sync(0xffffffffu, f != 1.f)) {
+          // O must include P_{j-1} V_{j-1} before it is rescaled.
+          if (!mbar_wait_bounded(&bar[B_PVDONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, WAIT_LIMIT))
+            ok = false;
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < CW / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        // P = 2^(s * scale_log2 - m_ref), packed to 16-bit pairs.
+        const float nmu = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        uint32_t pk[CW / 2];
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < CW / 2; ++c) {
+          const float x0 = fmaf(sv[2 * c], sl2, nmu), x1 = fmaf(sv[2 * c + 1], sl2, nmu);
+          const float p0 = (POLY_EVERY && (2 * c) % POLY_EVERY == POLY_EVERY - 1) ? exp2_fma(x0)
+                                                                               : fast_exp2(x0);
+          const float p1 = (POLY_EVERY && (2 * c + 1) % POLY_EVERY == POLY_EVERY - 1)
+                               ? exp2_fma(x1)
+                               : fast_exp2(x1);
+          ps[c & 3] += p0 + p1;
+          pk[c] = Mma<T>::pack(p0, p1);
+        }
+        l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+        // The P buffer is free once the P V product of two tiles ago completed.
+        if (g >= 2 && !mbar_wait_bounded(&bar[B_PVDONE + pb], ((g >> 1) - 1) & 1, WAIT_LIMIT))
+          ok = false;
+        if (__any_sync(0xffffffffu, !ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tp = tmem + COL_P + pb * 64 + lane_off + col0 / 2;
+        if constexpr (CW == 128) {
+          tmem_st32(tp, pk);
+          tmem_st32(tp + 32, pk + 32);
+        } else if constexpr (CW == 64) {
+          tmem_st32(tp, pk);
+        } else {
+          tmem_st16(tp, pk);
+        }
+        tmem_wait_st();
+        const int kbase = j * BN;
+        if (warp == 0 && kbase + BN > I.kv_len) {
+          // Last tile: zero the V rows of keys past the context (whole 128-byte
+          // rows of both halves) so p = 0 adds nothing even where an unwritten
+          // slot holds NaN.  Warp 0's p_full arrival orders it before P V.
+          const int st = g % KS;
+          if (!mbar_wait_bounded(&bar[B_VFULL + st], (g / KS) & 1, WAIT_LIMIT)) ok = false;
+          const uint32_t vb = base + OFF_V + st * TILE_BYTES;
+          const int first = max(0, I.kv_len - kbase);
+          for (int idx = lane; idx < (BN - first) * 16; idx += 32) {
+            const int r = first + idx / 16, c16 = idx % 16;
+            const uint32_t a = vb + (c16 >> 3) * HALF_BYTES + r * 128 + (c16 & 7) * 16;
+            asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+          }
+          fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_PFULL + pb]);
+      }
+      // Uniform: the epilogue below is warp-collective.
+      if (__any_sync(0xffffffffu, !ok)) {
+        ok = false;
+        break;
+      }
+      // ---------------------------------------------------------- epilogue
+      bool done = !*abort_flag && mbar_wait_bounded(&bar[B_OFULL], ic & 1, WAIT_LIMIT);
+      done = __all_sync(0xffffffffu, done);
+      if (!done) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[BN];
+      uint32_t o[CW];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS[b] + lane_off + c * 32,
-                                                  reinterpret_cast<uint32_t*>(sv + c * 32));
+      for (int c = 0; c < CW / 32; ++c) tmem_ld32(tO + c * 32, o + c * 32);
       tmem_wait_ld();
-      const int kbase = j * BN;
-      const bool full_tile = kbase + BN - 1 <= win_start + pos0 && kbase + BN <= kv_len;
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        float x = sv[c] * sl2;
-        if (!full_tile && (kbase + c > limit || kbase + c >= kv_len)) x = -INFINITY;
-        sv[c] = x;
-        tmax = fmaxf(tmax, x);
-      }
-      // Lazy rescale: a row keeps its reference max unless this tile exceeds it
-      // by more than 2^8.  The O correction is a warp-collective TMEM
-      // read-modify-write, done when any row of the warp needs it (the other
-      // rows multiply by 1).
-      float f = 1.f;
-      if (tmax != -INFINITY && (m_ref == -INFINITY || tmax > m_ref + RESCALE_THRESHOLD)) {
-        if (m_ref != -INFINITY) f = fast_exp2(m_ref - tmax);
-        m_ref = tmax;
-      }
-      l_sum *= f;
-      if (j > 0 && __any_sync(0xffffffffu, f != 1.f)) {
-        // O must include P_{j-1} V_{j-1} before it is rescaled.
-        if (!mbar_wait_bounded(bars.o_done(), (j - 1) & 1, WAIT_LIMIT)) ok = false;
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + lane_off + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-          tmem_st32(tO + lane_off + c * 32, o);
-        }
-      }
-      const float mu = (m_ref == -INFINITY) ? 0.f : m_ref;
-      uint32_t pk[BN / 2];
-      float psum = 0.f;
-#pragma unroll
-      for (int c = 0; c < BN / 2; ++c) {
-        const float p0 = fast_exp2(sv[2 * c] - mu), p1 = fast_exp2(sv[2 * c + 1] - mu);
-        psum += p0 + p1;
-        pk[c] = Mma<T>::pack(p0, p1);
-      }
-      l_sum += psum;
-      // P overwrites the first 64 columns of this S buffer (own lane only).
-      tmem_st32(tS[b] + lane_off, pk);
-      tmem_st32(tS[b] + lane_off + 32, pk + 32);
-      tmem_wait_st();
-      if (warp == 0 && kbase + BN > kv_len) {
-        // Last tile: zero the V rows of keys past the context (whole 128-byte
-        // rows of both halves) so p = 0 adds nothing even where an unwritten
-        // slot holds NaN.  Warp 0's p_full arrival orders it before P V.
-        const int st = j % STAGES;
-        if (!mbar_wait_bounded(bars.v_full(st), (j / STAGES) & 1, WAIT_LIMIT)) ok = false;
-        const uint32_t vb = base + OFF_V + st * TILE_BYTES;
-        const int first = max(0, kv_len - kbase);
-        for (int idx = lane; idx < (BN - first) * 16; idx += 32) {
-          const int r = first + idx / 16, c16 = idx % 16;
-          const uint32_t a = vb + (c16 >> 3) * HALF_BYTES + r * 128 + (c16 & 7) * 16;
-          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
-        }
-        fence_proxy_async_smem();
-      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bars.p_full(b));
-    }
-    // ---------------------------------------------------------- epilogue
-    bool done = ok && !*abort_flag && mbar_wait_bounded(bars.o_done(), (ntiles - 1) & 1, WAIT_LIMIT);
-    done = __all_sync(0xffffffffu, done);
-    if (done) {
-      tc_fence_after();
-      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      const bool valid = pos < q_len;
-      T* orow = static_cast<T*>(P.a.out) + (int64_t)(q_start + pos) * P.a.o_sr +
-                (int64_t)(h * G + g) * P.a.o_sh;
+      if (lane == 0) mbar_arrive(&bar[B_OFREE]);  // O may be overwritten
+      float l_tot;
+      if (!exchange(l_sum, false, l_tot)) {
+        ok = false;
+        break;
+      }
+      if (pos < I.q_len) {
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+        T* orow = static_cast<T*>(P.a.out) + (int64_t)(I.q_start + pos) * P.a.o_sr +
+                  (int64_t)(I.h * G + gg) * P.a.o_sh + col0;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + lane_off + c * 32, o);
-        tmem_wait_ld();
-        if (valid) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            uint4 v;
-            v.x = Mma<T>::pack(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
-            v.y = Mma<T>::pack(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
-            v.z = Mma<T>::pack(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
-            v.w = Mma<T>::pack(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + e) = v;
-          }
+        for (int e = 0; e < CW; e += 8) {
+          uint4 v;
+          v.x = Mma<T>::pack(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+          v.y = Mma<T>::pack(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+          v.z = Mma<T>::pack(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+          v.w = Mma<T>::pack(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + e) = v;
         }
       }
-    } else {
+    }
+    if (!ok) {
       if (lane == 0) set_err(P.a.err, MF_ERR_TIMEOUT);
       *abort_flag = 1;
     }
@@ -433,6 +638,7 @@ const char* prefill_tc_unsupported(const AttnParams& p, mf_dtype dtype) {
   const int G = p.hq / p.hkv;
   if (G > 8 || pf::BM % G) return "GQA group does not divide 128";
   if (p.wk || p.row_map) return "window / row_map";
+  if (p.num_seqs > pf::MAX_SEQS) return "more than 4096 sequences";
   if (!p.causal) return "non-causal";
   if ((int64_t)p.num_blocks * pf::PAGE > 0x7fffffffLL) return "pool slots exceed int32";
   return nullptr;
@@ -459,25 +665,27 @@ int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
   P.a = p;
   P.G = G;
   P.rows_cap = rows_cap;
-  P.q_tiles = (p.max_q_len * G + pf::BM - 1) / pf::BM;
   P.scale_log2 = p.scale * 1.4426950408889634f;
   P.in_fmt = dtype == MF_BF16 ? 1u : 0u;
-  const int64_t gx = (int64_t)p.num_seqs * P.q_tiles;
-  if (gx == 0) return MF_OK;
-  if (gx > 0x7fffffff || p.hkv > 65535) return fail(MF_EINVAL, "prefill: grid too large");
+  // Persistent grid: one CTA per SM, or fewer when there are fewer items
+  // (num_seqs x query tiles of the longest run x kv heads bounds the count).
+  const int64_t q_tiles = ((int64_t)p.max_q_len * G + pf::BM - 1) / pf::BM;
+  const int64_t items_max = (int64_t)p.num_seqs * q_tiles * p.hkv;
+  if (items_max == 0) return MF_OK;
+  const int64_t grid = std::min<int64_t>(items_max, current_sm_count());
   auto kern = dtype == MF_BF16 ? pf::prefill_kernel<__nv_bfloat16> : pf::prefill_kernel<__half>;
-  const size_t smem = pf::SMEM_BYTES + 1024;
+  const size_t smem = pf::smem_bytes(p.num_seqs) + 1024;
   static thread_local int configured_dev[2] = {-1, -1};
   int dev = 0;
   cudaGetDevice(&dev);
   const int which = dtype == MF_BF16 ? 1 : 0;
   if (configured_dev[which] != dev) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+                                         (int)(pf::smem_bytes(pf::MAX_SEQS) + 1024));
     if (e != cudaSuccess) return fail(MF_ECUDA, std::string("prefill: ") + cudaGetErrorString(e));
     configured_dev[which] = dev;
   }
-  kern<<<dim3((unsigned)gx, p.hkv), pf::THREADS, smem, stream>>>(mq, mk, mv, P);
+  kern<<<(unsigned)grid, pf::THREADS, smem, stream>>>(mq, mk, mv, P);
   return check_launch("paged attention (tcgen05 prefill)");
 }
 

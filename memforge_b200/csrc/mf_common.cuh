@@ -185,6 +185,23 @@ MF_DEVINL float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for x <= 8 on the FMA pipe, to share the exponentials of a softmax tile
+// with the SFU.  Range reduction: adding 1.5 * 2^23 rounds x to the nearest
+// integer n (held in the low mantissa bits of t), f = x - n lies in [-1/2, 1/2];
+// 2^f is a degree-3 polynomial whose coefficients were fitted here for minimum
+// relative error on [-1/2, 1/2] (iteratively reweighted least squares; max
+// relative error 7.5e-5, far below 16-bit rounding); n is added to the
+// exponent field as an integer.  Inputs below -126 give 2^-126 or less.
+MF_DEVINL float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(0.05517149344086647f, f, 0.24261093139648438f);
+  p = fmaf(p, f, 0.6932609677314758f);
+  p = fmaf(p, f, 0.9999280571937561f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 }  // namespace mf
 
 // ------------------------------------------------------- tcgen05 / TMEM (sm_100a)
@@ -257,6 +274,21 @@ MF_DEVINL void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+MF_DEVINL void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+// Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32).
+MF_DEVINL void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (Blackwell layout: version 1).
