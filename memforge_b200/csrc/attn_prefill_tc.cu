@@ -9,17 +9,22 @@
 //              (tile rows) and columns [CW (w / 4), CW (w / 4 + 1)) of S, P and O;
 //              the WPQ warps of one lane quarter combine their partial row maxima
 //              (and, at the end, row sums) through shared memory
-//   next 2     TMA producers: Q (two buffers) and K, and V; per 128-key tile
-//              8 pages x 2 halves (4-D tiled loads from the pool, 128-byte
-//              swizzled) into two-stage K and V rings
-//   last warp  MMA issuer (one thread): S = Q K^T into one of two TMEM S buffers,
-//              O += P V with P read from one of two TMEM P buffers
+//   next 2     TMA producer warps: Q (two buffers) and K, and V; per 128-key
+//              tile 8 pages x 2 halves (4-D tiled loads from the pool, 128-byte
+//              swizzled), one box per lane, into two-stage K and V rings
+//   next warp  S issuer (one thread): S = Q K^T into one of two TMEM S buffers
+//   last warp  P V issuer (one thread): O += P V with P read from one of two
+//              TMEM P buffers
+//
+// tcgen05.mma issue returns only as the tensor pipe takes the instruction, so
+// one thread issuing everything would leave the pipe idle whenever it waits
+// (for a P, a K tile, a free buffer).  Two issuers, one per product, let each
+// keep the pipe busy while the other waits.
 //
 // TMEM (512 columns): S_a S_b (128 fp32 each), P_a P_b (64 columns of packed
 // 16-bit pairs each), O (128 fp32).  P does not alias S, so an S buffer is free
-// again as soon as the softmax warps have loaded it, and the MMA issue order
-// S_0 S_1 P_0V_0 S_2 P_1V_1 S_3 ... (across work items too) keeps the next S
-// and the previous P V queued on the tensor pipe while a tile's softmax runs.
+// again as soon as the softmax warps have loaded it: the S of a tile can be
+// computed while the softmax of the previous tile runs.
 //
 // The online softmax keeps a per-row reference max (log2 units) and only
 // rescales O (a TMEM read-modify-write) when a tile's max exceeds it by more
@@ -43,8 +48,9 @@ constexpr int BN = 128;
 constexpr int WPQ = 1;                  // softmax warps per TMEM lane quarter
 constexpr int SM_WARPS = 4 * WPQ;       // softmax warps
 constexpr int CW = BN / WPQ;            // score columns per softmax warp
-constexpr int TMA_WARP = SM_WARPS, V_WARP = SM_WARPS + 1, MMA_WARP = SM_WARPS + 2;
-constexpr int THREADS = (SM_WARPS + 3) * 32;
+constexpr int TMA_WARP = SM_WARPS, V_WARP = SM_WARPS + 1, MMA_WARP = SM_WARPS + 2,
+              PV_WARP = SM_WARPS + 3;
+constexpr int THREADS = (SM_WARPS + 4) * 32;
 // One exponential in POLY_EVERY runs on the FMA pipe (exp2_fma), the rest on
 // the SFU; 0 keeps them all on the SFU.
 constexpr int POLY_EVERY = 0;
@@ -65,9 +71,14 @@ constexpr uint32_t OFF_V = OFF_K + KS * TILE_BYTES;
 constexpr uint32_t OFF_BAR = OFF_V + KS * TILE_BYTES;
 
 // mbarrier indices
-constexpr int B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_KEMPTY = B_KFULL + KS,
-              B_VFULL = B_KEMPTY + KS, B_VEMPTY = B_VFULL + KS, B_SFULL = B_VEMPTY + KS,
-              B_SFREE = B_SFULL + 2, B_PFULL = B_SFREE + 2, B_PVDONE = B_PFULL + 2,
+// S_DONE[b] (the S of tile g completed, b = g & 1) also frees K ring stage
+// g % KS, and PV_DONE[b] (the P V of tile g completed) also frees P buffer b and
+// V ring stage g % KS: with two stages the indices coincide, so one commit
+// serves both waiters.
+static_assert(KS == 2, "ring stages double as S / P buffer indices");
+constexpr int B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_VFULL = B_KFULL + KS,
+              B_SDONE = B_VFULL + KS, B_SFREE = B_SDONE + 2, B_PFULL = B_SFREE + 2,
+              B_PVDONE = B_PFULL + 2,
               B_OFULL = B_PVDONE + 2, B_OFREE = B_OFULL + 1, B_IDLE = B_OFREE + 1,
               B_XCH = B_IDLE + 1, NBAR = B_XCH + 4;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
@@ -148,20 +159,18 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar[B_QFULL + i], 1);
       mbar_init(&bar[B_QEMPTY + i], 1);
-      mbar_init(&bar[B_SFULL + i], 1);
+      mbar_init(&bar[B_SDONE + i], 1);
       mbar_init(&bar[B_SFREE + i], SM_WARPS);
       mbar_init(&bar[B_PFULL + i], SM_WARPS);
       mbar_init(&bar[B_PVDONE + i], 1);
     }
     for (int st = 0; st < KS; ++st) {
       mbar_init(&bar[B_KFULL + st], 1);
-      mbar_init(&bar[B_KEMPTY + st], 1);
       mbar_init(&bar[B_VFULL + st], 1);
-      mbar_init(&bar[B_VEMPTY + st], 1);
     }
     mbar_init(&bar[B_OFULL], 1);
     mbar_init(&bar[B_OFREE], SM_WARPS);
-    mbar_init(&bar[B_IDLE], 1);
+    mbar_init(&bar[B_IDLE], 2);  // one commit per issuer
     for (int q = 0; q < 4; ++q) mbar_init(&bar[B_XCH + q], WPQ);
     *abort_flag = 0;
     fence_barrier_init();
@@ -212,88 +221,95 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
   if (warp == TMA_WARP || warp == V_WARP) {
     // ======================================================= TMA producers
     // One warp loads Q and K, another V: the K ring frees at S completion and
-    // the V ring only at P V completion, so K loads never queue behind V.
+    // the V ring only at P V completion, so K loads never queue behind V.  A
+    // 128-key tile is 8 pages x 2 halves = 16 boxes: lane l < 16 loads the block
+    // id of page l / 2 (one tile ahead) and issues the box of (page l / 2, half
+    // l % 2), so a tile goes out as one warp instruction; lane 0 does the ring
+    // waits and the transaction count, and broadcasts every decision.
+    const bool is_v = warp == V_WARP;
+    const uint64_t pol_once = l2_evict_first_policy();
+    const uint64_t pol_keep = l2_evict_last_policy();
     if (lane == 0) {
-      const bool is_v = warp == V_WARP;
-      const uint64_t pol_once = l2_evict_first_policy();
-      const uint64_t pol_keep = l2_evict_last_policy();
       if (!is_v) {
         prefetch_tmap(&tmq);
         prefetch_tmap(&tmk);
       } else {
         prefetch_tmap(&tmv);
       }
-      const CUtensorMap* tmap = is_v ? &tmv : &tmk;
-      const uint32_t ring = is_v ? OFF_V : OFF_K;
-      uint64_t* fullb = &bar[is_v ? B_VFULL : B_KFULL];
-      uint64_t* emptyb = &bar[is_v ? B_VEMPTY : B_KEMPTY];
-      const int nb = P.a.num_blocks;
-      uint32_t g = 0;      // tiles started (all items)
-      uint32_t armed = 0;  // tiles whose loads were issued
-      int ic = 0;          // items whose Q load was issued (lane 0)
-      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-        const Item I = item_at(P, prefix, B, it);
-        if (!is_v) {
-          const int qb = ic & 1;
+    }
+    const CUtensorMap* tmap = is_v ? &tmv : &tmk;
+    const uint32_t ring = is_v ? OFF_V : OFF_K;
+    uint64_t* fullb = &bar[is_v ? B_VFULL : B_KFULL];
+    uint64_t* emptyb = &bar[is_v ? B_PVDONE : B_SDONE];  // ring stage g % KS frees
+    const int nb = P.a.num_blocks;
+    const bool boxer = lane < 2 * (BN / PAGE);
+    const int my_pg = lane >> 1, my_half = lane & 1;
+    uint32_t g = 0;      // tiles started (all items)
+    uint32_t armed = 0;  // tiles whose loads were issued
+    int ic = 0;          // items whose Q load was issued
+    bool run = true;
+    for (int it = blockIdx.x; run && it < items; it += gridDim.x) {
+      run = __shfl_sync(0xffffffffu, *abort_flag == 0, 0);
+      if (!run) break;
+      const Item I = item_at(P, prefix, B, it);
+      if (!is_v) {
+        const int qb = ic & 1;
+        bool fine = true;
+        if (lane == 0) {
           if (ic >= 2 &&
               !mbar_wait_bounded(&bar[B_QEMPTY + qb], ((ic >> 1) - 1) & 1, WAIT_LIMIT)) {
             set_err(P.a.err, MF_ERR_TIMEOUT);
             *abort_flag = 1;
-            break;
+            fine = false;
+          } else {
+            mbar_arrive_expect_tx(&bar[B_QFULL + qb], TILE_BYTES);
+            for (int half = 0; half < 2; ++half)
+              tma_load_4d(gbase + OFF_Q + qb * TILE_BYTES + half * HALF_BYTES, &tmq,
+                          &bar[B_QFULL + qb], 0, I.h * G, half, I.q_start + I.pos0, pol_once);
           }
-          mbar_arrive_expect_tx(&bar[B_QFULL + qb], TILE_BYTES);
-          for (int half = 0; half < 2; ++half)
-            tma_load_4d(gbase + OFF_Q + qb * TILE_BYTES + half * HALF_BYTES, &tmq,
-                        &bar[B_QFULL + qb], 0, I.h * G, half, I.q_start + I.pos0, pol_once);
-          ++ic;
         }
-        const int pool_pages = (I.kv_len + PAGE - 1) / PAGE;
-        const int32_t* table = P.a.tables + (int64_t)I.s * P.a.table_stride;
-        // Block ids of a tile's 8 pages, loaded one tile ahead (independent
-        // loads, consumed a tile later) so the table reads stay off the TMA
-        // issue path.  Out-of-table pages use an out-of-range coordinate: TMA
-        // fills zeros.
-        auto load_ids = [&](int j, int* ids) {
-#pragma unroll
-          for (int pg = 0; pg < BN / PAGE; ++pg) {
-            const int L = j * (BN / PAGE) + pg;
-            ids[pg] = L < pool_pages ? __ldg(table + L) : -1;
-          }
-        };
-        int nxt[BN / PAGE];
-        load_ids(0, nxt);
-        for (int j = 0; j < I.nt; ++j, ++g) {
-          int tok[BN / PAGE];
-#pragma unroll
-          for (int pg = 0; pg < BN / PAGE; ++pg) {
-            const int L = j * (BN / PAGE) + pg;
-            tok[pg] = nb * PAGE;
-            if (L < pool_pages) {
-              if (nxt[pg] >= 0 && nxt[pg] < nb) tok[pg] = nxt[pg] * PAGE;
-              else set_err(P.a.err, MF_ERR_BLOCK_ID);
-            }
-          }
-          if (j + 1 < I.nt) load_ids(j + 1, nxt);
-          const int st = g % KS;
+        run = __shfl_sync(0xffffffffu, fine, 0);
+        if (!run) break;
+        ++ic;
+      }
+      const int pool_pages = (I.kv_len + PAGE - 1) / PAGE;
+      const int32_t* table = P.a.tables + (int64_t)I.s * P.a.table_stride;
+      // Block id of this lane's page, loaded one tile ahead.  Out-of-table
+      // pages use an out-of-range coordinate: TMA fills zeros.
+      int nxt = (boxer && my_pg < pool_pages) ? __ldg(table + my_pg) : -1;
+      for (int j = 0; j < I.nt; ++j, ++g) {
+        const int L = j * (BN / PAGE) + my_pg;
+        int tok = nb * PAGE;
+        if (boxer && L < pool_pages) {
+          if (nxt >= 0 && nxt < nb) tok = nxt * PAGE;
+          else set_err(P.a.err, MF_ERR_BLOCK_ID);
+        }
+        if (j + 1 < I.nt)
+          nxt = (boxer && L + BN / PAGE < pool_pages) ? __ldg(table + L + BN / PAGE) : -1;
+        const int st = g % KS;
+        bool fine = true;
+        if (lane == 0) {
           if (g >= KS && !mbar_wait_bounded(&emptyb[st], ((g / KS) - 1) & 1, WAIT_LIMIT)) {
             set_err(P.a.err, MF_ERR_TIMEOUT);
             *abort_flag = 1;
-            break;
+            fine = false;
+          } else if (*abort_flag) {
+            fine = false;
+          } else {
+            mbar_arrive_expect_tx(&fullb[st], TILE_BYTES);
           }
-          if (*abort_flag) break;
-          mbar_arrive_expect_tx(&fullb[st], TILE_BYTES);
-          armed = g + 1;
-          uint8_t* dst = gbase + ring + st * TILE_BYTES;
-#pragma unroll
-          for (int pg = 0; pg < BN / PAGE; ++pg)
-#pragma unroll
-            for (int half = 0; half < 2; ++half)
-              tma_load_4d(dst + half * HALF_BYTES + pg * PAGE * 128, tmap, &fullb[st], 0,
-                          tok[pg], half, I.h, pol_keep);
         }
+        run = __shfl_sync(0xffffffffu, fine, 0);  // also orders expect_tx before the loads
+        if (!run) break;
+        armed = g + 1;
+        if (boxer)
+          tma_load_4d(gbase + ring + st * TILE_BYTES + my_half * HALF_BYTES + my_pg * PAGE * 128,
+                      tmap, &fullb[st], 0, tok, my_half, I.h, pol_keep);
       }
-      // Drain every armed load before the CTA can exit (the ring holds the
-      // last KS tiles and, for lane 0, the last two Q tiles in flight at most).
+    }
+    // Drain every armed load before the CTA can exit (the ring holds the last
+    // KS tiles and the last two Q tiles in flight at most).
+    if (lane == 0) {
       for (uint32_t k = armed > (uint32_t)KS ? armed - KS : 0u; k < armed; ++k)
         if (!mbar_wait_bounded(&fullb[k % KS], (k / KS) & 1, WAIT_LIMIT))
           set_err(P.a.err, MF_ERR_TIMEOUT);
@@ -302,76 +318,65 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
           if (!mbar_wait_bounded(&bar[B_QFULL + (i & 1)], (i >> 1) & 1, WAIT_LIMIT))
             set_err(P.a.err, MF_ERR_TIMEOUT);
     }
-  } else if (warp == MMA_WARP) {
-    // ========================================================= MMA issuer
+  } else if (warp == MMA_WARP || warp == PV_WARP) {
+    // ========================================================= MMA issuers
     if (lane == 0) {
+      const bool is_pv = warp == PV_WARP;
       const uint32_t idesc_s = idesc_f16(BM, BN, P.in_fmt, false);
       const uint32_t idesc_o = idesc_f16(BM, D, P.in_fmt, true);
       const uint32_t tO = tmem + COL_O;
       bool ok = true;
-      // The P V product of one tile is issued after the S of the next tile.
-      bool pend = false;
-      uint32_t pg_ = 0;  // pending tile (global index)
-      int p_first = 0, p_last = 0, p_item = 0;
-      auto issue_pv = [&]() {
-        const int pb = pg_ & 1, st = pg_ % KS;
-        ok = ok && mbar_wait_bounded(&bar[B_PFULL + pb], (pg_ >> 1) & 1, WAIT_LIMIT);
-        ok = ok && mbar_wait_bounded(&bar[B_VFULL + st], (pg_ / KS) & 1, WAIT_LIMIT);
-        // The first P V of an item overwrites O: the previous epilogue must have read it.
-        if (p_first && p_item > 0)
-          ok = ok && mbar_wait_bounded(&bar[B_OFREE], (p_item - 1) & 1, WAIT_LIMIT);
-        if (!ok || *abort_flag) return;
-        tc_fence_after();
-        const uint32_t vb = base + OFF_V + st * TILE_BYTES;
-#pragma unroll
-        for (int ks = 0; ks < BN / 16; ++ks)
-          // P columns ks*8 .. (16 keys packed 2 per column); V rows ks*16 ..
-          umma_ts(tO, tmem + COL_P + pb * 64 + ks * 8,
-                  sdesc_sw128(vb + ks * 16 * 128, HALF_BYTES, 1024), idesc_o,
-                  (p_first && ks == 0) ? 0u : 1u);
-        umma_commit(&bar[B_VEMPTY + st]);
-        umma_commit(&bar[B_PVDONE + pb]);
-        if (p_last) umma_commit(&bar[B_OFULL]);
-        pend = false;
-      };
       uint32_t g = 0;
       int ic = 0;
       for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++ic) {
         const Item I = item_at(P, prefix, B, it);
         const int qb = ic & 1;
-        ok = mbar_wait_bounded(&bar[B_QFULL + qb], (ic >> 1) & 1, WAIT_LIMIT);
+        if (!is_pv) ok = mbar_wait_bounded(&bar[B_QFULL + qb], (ic >> 1) & 1, WAIT_LIMIT);
         const uint32_t qbase = base + OFF_Q + qb * TILE_BYTES;
         for (int j = 0; ok && j < I.nt; ++j, ++g) {
-          const int sb = g & 1, st = g % KS;
-          if (g >= 2) ok = ok && mbar_wait_bounded(&bar[B_SFREE + sb], ((g >> 1) - 1) & 1, WAIT_LIMIT);
-          ok = ok && mbar_wait_bounded(&bar[B_KFULL + st], (g / KS) & 1, WAIT_LIMIT);
-          if (!ok || *abort_flag) break;
-          tc_fence_after();
-          const uint32_t kb = base + OFF_K + st * TILE_BYTES;
+          const int b2 = g & 1, st = g % KS;
+          if (!is_pv) {
+            // S_g = Q K_g^T once the softmax has loaded the S of tile g - 2.
+            if (g >= 2)
+              ok = ok && mbar_wait_bounded(&bar[B_SFREE + b2], ((g >> 1) - 1) & 1, WAIT_LIMIT);
+            ok = ok && mbar_wait_bounded(&bar[B_KFULL + st], (g / KS) & 1, WAIT_LIMIT);
+            if (!ok || *abort_flag) break;
+            tc_fence_after();
+            const uint32_t kb = base + OFF_K + st * TILE_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * HALF_BYTES + (ks & 3) * 32;
-            umma_ss(tmem + COL_S + sb * 128, sdesc_sw128(qbase + off, 16, 1024),
-                    sdesc_sw128(kb + off, 16, 1024), idesc_s, ks > 0);
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint32_t off = (ks >> 2) * HALF_BYTES + (ks & 3) * 32;
+              umma_ss(tmem + COL_S + b2 * 128, sdesc_sw128(qbase + off, 16, 1024),
+                      sdesc_sw128(kb + off, 16, 1024), idesc_s, ks > 0);
+            }
+            umma_commit(&bar[B_SDONE + b2]);
+            if (j == I.nt - 1) umma_commit(&bar[B_QEMPTY + qb]);
+          } else {
+            // O += P_g V_g; the first P V of an item overwrites O, after the
+            // previous epilogue has read it.
+            ok = ok && mbar_wait_bounded(&bar[B_PFULL + b2], (g >> 1) & 1, WAIT_LIMIT);
+            ok = ok && mbar_wait_bounded(&bar[B_VFULL + st], (g / KS) & 1, WAIT_LIMIT);
+            if (j == 0 && ic > 0)
+              ok = ok && mbar_wait_bounded(&bar[B_OFREE], (ic - 1) & 1, WAIT_LIMIT);
+            if (!ok || *abort_flag) break;
+            tc_fence_after();
+            const uint32_t vb = base + OFF_V + st * TILE_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < BN / 16; ++ks)
+              // P columns ks*8 .. (16 keys packed 2 per column); V rows ks*16 ..
+              umma_ts(tO, tmem + COL_P + b2 * 64 + ks * 8,
+                      sdesc_sw128(vb + ks * 16 * 128, HALF_BYTES, 1024), idesc_o,
+                      (j == 0 && ks == 0) ? 0u : 1u);
+            umma_commit(&bar[B_PVDONE + b2]);
+            if (j == I.nt - 1) umma_commit(&bar[B_OFULL]);
           }
-          umma_commit(&bar[B_KEMPTY + st]);
-          umma_commit(&bar[B_SFULL + sb]);
-          if (j == I.nt - 1) umma_commit(&bar[B_QEMPTY + qb]);
-          if (pend) issue_pv();
-          if (!ok || *abort_flag) break;
-          pend = true;
-          pg_ = g;
-          p_first = j == 0;
-          p_last = j == I.nt - 1;
-          p_item = ic;
         }
       }
-      if (ok && pend && !*abort_flag) issue_pv();
       if (!ok) {
         set_err(P.a.err, MF_ERR_TIMEOUT);
         *abort_flag = 1;
       }
-      // Every MMA issued above has completed before TMEM can be freed.
+      // Every MMA either thread issued has completed before TMEM can be freed.
       umma_commit(&bar[B_IDLE]);
       if (!mbar_wait_bounded(&bar[B_IDLE], 0, WAIT_LIMIT)) set_err(P.a.err, MF_ERR_TIMEOUT);
     }
@@ -416,7 +421,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
       float m_ref = -INFINITY, l_sum = 0.f;
       for (int j = 0; j < I.nt; ++j, ++g) {
         const int sb = g & 1, pb = g & 1;
-        if (!mbar_wait_bounded(&bar[B_SFULL + sb], (g >> 1) & 1, WAIT_LIMIT)) ok = false;
+        if (!mbar_wait_bounded(&bar[B_SDONE + sb], (g >> 1) & 1, WAIT_LIMIT)) ok = false;
         // Warp-uniform decision: tcgen05.ld/st below are warp-collective.
         if (__any_sync(0xffffffffu, !ok || *abort_flag != 0)) {
           ok = false;
@@ -440,13 +445,14 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
           for (int c = 0; c < CW; ++c)
             if (c > lim) sv[c] = -INFINITY;
         }
+        // Eight independent chains of three-input maxima (two new columns each).
         float mx[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = sv[e];
 #pragma unroll
-        for (int c = 8; c < CW; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
-        float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                           fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+        for (int c = 8; c < CW; c += 2) mx[(c >> 1) & 7] = fmax3f(mx[(c >> 1) & 7], sv[c], sv[c + 1]);
+        float mraw = fmax3f(fmax3f(mx[0], mx[1], mx[2]), fmax3f(mx[3], mx[4], mx[5]),
+                            fmaxf(mx[6], mx[7]));
         if (!exchange(mraw, true, mraw)) {
           ok = false;
           break;

@@ -178,6 +178,13 @@ template <> struct Mma<__half> {
   }
 };
 
+// max(a, b, c) in one instruction (three-input max, sm_100).
+MF_DEVINL float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // 2^x on the SFU (the flash-attention formulation works in the log2 domain).
 MF_DEVINL float fast_exp2(float x) {
   float y;
