@@ -346,8 +346,8 @@ def run_ours(args):
 
 
 # Per-launch DRAM bytes (read + write) of the decode kernel at this workload from
-# one ncu capture (profiles/decode_cfg2.md: 583.016 MB read + 4.847 MB written).
-TRAFFIC_BYTES = {"cfg2": 587863808}
+# one ncu capture (profiles/decode_cfg2.md: 583.214 MB read + 6.235 MB written).
+TRAFFIC_BYTES = {"cfg2": 589448704}
 
 
 def capture_graph(fn, dev):
