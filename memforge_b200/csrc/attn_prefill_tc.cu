@@ -51,9 +51,6 @@ constexpr int CW = BN / WPQ;            // score columns per softmax warp
 constexpr int TMA_WARP = SM_WARPS, V_WARP = SM_WARPS + 1, MMA_WARP = SM_WARPS + 2,
               PV_WARP = SM_WARPS + 3;
 constexpr int THREADS = (SM_WARPS + 4) * 32;
-// One exponential in POLY_EVERY runs on the FMA pipe (exp2_fma), the rest on
-// the SFU; 0 keeps them all on the SFU.
-constexpr int POLY_EVERY = 0;
 static_assert(CW == 32 || CW == 64 || CW == 128, "softmax column split");
 constexpr int D = 128;
 constexpr int PAGE = 16;
@@ -85,13 +82,41 @@ constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
 // Row-statistic exchange between the softmax warps of a lane quarter: two
 // buffers of [WPQ][BM] floats.
 constexpr uint32_t OFF_XCH = OFF_MISC + 16;
-constexpr uint32_t OFF_PREFIX = OFF_XCH + 2 * WPQ * BM * 4;  // int[num_seqs + 1]
+// Work-list tables: prefix int[num_seqs + 1] (query tiles before the k-th
+// sequence in longest-first order), order uint16[num_seqs] (that sequence), and
+// NBK bucket counters of the counting sort.
+constexpr uint32_t OFF_PREFIX = OFF_XCH + 2 * WPQ * BM * 4;
+constexpr int NBK = 256;
 
 // TMEM column offsets
 constexpr uint32_t COL_S = 0, COL_P = 256, COL_O = 384;
 
+__host__ __device__ constexpr uint32_t off_order(int num_seqs) {
+  return OFF_PREFIX + (((uint32_t)(num_seqs + 1) * 4u + 15u) & ~15u);
+}
+__host__ __device__ constexpr uint32_t off_counts(int num_seqs) {
+  return off_order(num_seqs) + (((uint32_t)num_seqs * 2u + 15u) & ~15u);
+}
 __host__ __device__ constexpr uint32_t smem_bytes(int num_seqs) {
-  return OFF_PREFIX + (uint32_t)(num_seqs + 1) * 4u;
+  return off_counts(num_seqs) + NBK * 4u;
+}
+static_assert(smem_bytes(MAX_SEQS) + 1024 <= 227u * 1024u, "shared memory budget");
+
+// Sort key of a sequence: about 8 buckets per doubling of kv_len, longest first
+// (bucket 0); sequences without work last.
+MF_DEVINL int length_bucket(int kv_len, int tiles) {
+  if (tiles == 0 || kv_len <= 0) return NBK - 1;
+  const int e = 31 - __clz(kv_len);
+  const int mant = e >= 3 ? (kv_len >> (e - 3)) & 7 : (kv_len << (3 - e)) & 7;
+  return NBK - 2 - min(8 * e + mant, NBK - 2);
+}
+
+// Work item handled by this CTA in its k-th step: items are dealt to the CTAs
+// in a snake order (0..G-1, then G-1..0, ...), so that with the longest items
+// first the CTAs that get the longest of one pass get the shortest of the next.
+MF_DEVINL int snake_item(int k) {
+  const int G = gridDim.x, c = blockIdx.x;
+  return k * G + ((k & 1) ? G - 1 - c : c);
 }
 
 struct Params {
@@ -100,12 +125,18 @@ struct Params {
   int rows_cap;      // sequences with q_len * G <= rows_cap belong to the decode kernel
   float scale_log2;
   uint32_t in_fmt;   // 0 = f16, 1 = bf16
+  int window;        // 1: the last q_len keys of each sequence come from the window buffers
 };
 
 // Geometry of one work item (identical in every role).
 struct Item {
   int s, h, q_start, q_len, kv_len, win_start, pos0, nt;
+  int pool_len;  // keys read from the pool (the rest, with a window, from the window buffers)
 };
+
+// Query positions per tile: the tile's rows are (position, query head) pairs,
+// floor(128 / G) positions x G heads (the rows past that are padding).
+__host__ __device__ constexpr int positions_per_tile(int G) { return BM / G; }
 
 MF_DEVINL int find_tile_seq(const int* prefix, int B, int t) {
   int lo = 0, hi = B;  // prefix[lo] <= t < prefix[hi]
@@ -116,31 +147,41 @@ MF_DEVINL int find_tile_seq(const int* prefix, int B, int t) {
   return lo;
 }
 
-// Items are ordered so that the tiles with the most keys (the last tiles of
-// each sequence) come first.
-MF_DEVINL Item item_at(const Params& P, const int* prefix, int B, int it) {
+// Items run longest first: sequences by decreasing kv_len, and within a
+// sequence the last query tiles (which see the most keys) first.
+MF_DEVINL Item item_at(const Params& P, const int* prefix, const uint16_t* order, int B,
+                       int it) {
   Item I;
   const int hkv = P.a.hkv;
-  const int T = prefix[B];
-  const int t = T - 1 - it / hkv;
+  const int t = it / hkv;
   I.h = it % hkv;
-  I.s = find_tile_seq(prefix, B, t);
-  const int qt = t - prefix[I.s];
+  const int k = find_tile_seq(prefix, B, t);
+  I.s = order[k];
+  const int qt = prefix[k + 1] - 1 - t;
   seq_rows(P.a, I.s, I.q_start, I.q_len);
   I.kv_len = __ldg(P.a.kv_lens + I.s);
   I.win_start = I.kv_len - I.q_len;
-  const int ppt = BM / P.G;
+  const int ppt = positions_per_tile(P.G);
   I.pos0 = qt * ppt;
   const int pos_last = min(I.q_len - 1, I.pos0 + ppt - 1);
-  const int key_end = I.win_start + pos_last + 1;  // keys this tile can see
-  I.nt = (key_end + BN - 1) / BN;
+  if (P.window) {
+    // Pool tiles for positions < kv_len - q_len, then one tile holding the
+    // window (q_len <= 16 keys) in its first rows.
+    I.pool_len = I.win_start;
+    I.nt = (I.pool_len + BN - 1) / BN + 1;
+  } else {
+    I.pool_len = I.kv_len;
+    const int key_end = I.win_start + pos_last + 1;  // keys this tile can see
+    I.nt = (key_end + BN - 1) / BN;
+  }
   return I;
 }
 
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
-    const __grid_constant__ CUtensorMap tmv, const __grid_constant__ Params P) {
+    const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tmwk,
+    const __grid_constant__ CUtensorMap tmwv, const __grid_constant__ Params P) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_base = smem_u32(smem_raw);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
@@ -149,6 +190,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + OFF_MISC + 4);
   int* prefix = reinterpret_cast<int*>(gbase + OFF_PREFIX);
+  uint16_t* order = reinterpret_cast<uint16_t*>(gbase + off_order(P.a.num_seqs));
+  int* counts = reinterpret_cast<int*>(gbase + off_counts(P.a.num_seqs));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int B = P.a.num_seqs;
@@ -175,28 +218,82 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     *abort_flag = 0;
     fence_barrier_init();
   }
-  // Query tiles per sequence: only runs longer than rows_cap rows are served here.
-  for (int i = tid; i < B; i += THREADS) {
-    int qs, ql;
-    seq_rows(P.a, i, qs, ql);
-    int tiles = 0;
-    if (ql > 0 && ql * G > P.rows_cap) {
-      const int kvl = P.a.kv_lens[i];
-      if (kvl < ql) {
-        set_err(P.a.err, MF_ERR_LENGTH);
-      } else if ((kvl + PAGE - 1) / PAGE > P.a.table_stride) {
-        set_err(P.a.err, MF_ERR_TABLE);
-      } else {
-        tiles = (ql * G + BM - 1) / BM;
-      }
-    }
-    prefix[i + 1] = tiles;
-  }
+  for (int i = tid; i < NBK; i += THREADS) counts[i] = 0;
   if (warp == 0) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
+  __syncthreads();
+  // Query tiles per sequence (only runs longer than rows_cap rows are served
+  // here) and a counting sort of the sequences by kv_len, longest first.  Every
+  // CTA builds the same list, so the sort is stable (ties keep index order).
+  for (int i = tid; i < B; i += THREADS) {
+    int qs, ql;
+    seq_rows(P.a, i, qs, ql);
+    int tiles = 0;
+    const int kvl = P.a.kv_lens[i];
+    if (ql > 0 && ql * G > P.rows_cap) {
+      if (kvl < ql) {
+        set_err(P.a.err, MF_ERR_LENGTH);
+      } else if (((P.window ? kvl - ql : kvl) + PAGE - 1) / PAGE > P.a.table_stride) {
+        set_err(P.a.err, MF_ERR_TABLE);
+      } else {
+        const int ppt = positions_per_tile(G);
+        tiles = (ql + ppt - 1) / ppt;
+      }
+    }
+    atomicAdd(&counts[length_bucket(kvl, tiles)], 1);
+    prefix[i + 1] = tiles;
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive scan of the bucket counts
+    int run = 0;
+    for (int c0 = 0; c0 < NBK; c0 += 32) {
+      int v = counts[c0 + lane];
+      const int own = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      counts[c0 + lane] = run + v - own;
+      run += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {  // place the sequences 32 at a time, in index order
+    for (int c0 = 0; c0 < B; c0 += 32) {
+      const int i = c0 + lane;
+      const int b = i < B ? length_bucket(P.a.kv_lens[i], prefix[i + 1]) : -1;
+      const unsigned same = __match_any_sync(0xffffffffu, b);
+      const int slot = b >= 0 ? counts[b] + __popc(same & ((1u << lane) - 1u)) : 0;
+      __syncwarp();
+      if (b >= 0) {
+        order[slot] = (uint16_t)i;
+        if (lane == __ffs(same) - 1) counts[b] += __popc(same);
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // Tiles per sequence in sorted order (all read before any is overwritten),
+  // then their prefix sums.
+  {
+    constexpr int NR = (MAX_SEQS + THREADS - 1) / THREADS;
+    int tv[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const int k = r * THREADS + tid;
+      tv[r] = k < B ? prefix[order[k] + 1] : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const int k = r * THREADS + tid;
+      if (k < B) prefix[k + 1] = tv[r];
+    }
+  }
   __syncthreads();
   if (warp == 0) {
     int run = 0;
@@ -227,6 +324,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     // l % 2), so a tile goes out as one warp instruction; lane 0 does the ring
     // waits and the transaction count, and broadcasts every decision.
     const bool is_v = warp == V_WARP;
+    const uint32_t q_bytes = (uint32_t)(positions_per_tile(G) * G) * D * 2;  // both halves
+    const CUtensorMap* wmap = is_v ? &tmwv : &tmwk;
     const uint64_t pol_once = l2_evict_first_policy();
     const uint64_t pol_keep = l2_evict_last_policy();
     if (lane == 0) {
@@ -236,6 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
       } else {
         prefetch_tmap(&tmv);
       }
+      if (P.window) prefetch_tmap(wmap);
     }
     const CUtensorMap* tmap = is_v ? &tmv : &tmk;
     const uint32_t ring = is_v ? OFF_V : OFF_K;
@@ -248,10 +348,10 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     uint32_t armed = 0;  // tiles whose loads were issued
     int ic = 0;          // items whose Q load was issued
     bool run = true;
-    for (int it = blockIdx.x; run && it < items; it += gridDim.x) {
+    for (int k = 0; run && snake_item(k) < items; ++k) {
       run = __shfl_sync(0xffffffffu, *abort_flag == 0, 0);
       if (!run) break;
-      const Item I = item_at(P, prefix, B, it);
+      const Item I = item_at(P, prefix, order, B, snake_item(k));
       if (!is_v) {
         const int qb = ic & 1;
         bool fine = true;
@@ -262,7 +362,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
             *abort_flag = 1;
             fine = false;
           } else {
-            mbar_arrive_expect_tx(&bar[B_QFULL + qb], TILE_BYTES);
+            mbar_arrive_expect_tx(&bar[B_QFULL + qb], q_bytes);
             for (int half = 0; half < 2; ++half)
               tma_load_4d(gbase + OFF_Q + qb * TILE_BYTES + half * HALF_BYTES, &tmq,
                           &bar[B_QFULL + qb], 0, I.h * G, half, I.q_start + I.pos0, pol_once);
@@ -272,7 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         if (!run) break;
         ++ic;
       }
-      const int pool_pages = (I.kv_len + PAGE - 1) / PAGE;
+      const int pool_pages = (I.pool_len + PAGE - 1) / PAGE;
       const int32_t* table = P.a.tables + (int64_t)I.s * P.a.table_stride;
       // Block id of this lane's page, loaded one tile ahead.  Out-of-table
       // pages use an out-of-range coordinate: TMA fills zeros.
@@ -287,6 +387,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         if (j + 1 < I.nt)
           nxt = (boxer && L + BN / PAGE < pool_pages) ? __ldg(table + L + BN / PAGE) : -1;
         const int st = g % KS;
+        // With a window, the last tile is the window: 16 rows of each half.
+        const bool win_tile = P.window && j == I.nt - 1;
         bool fine = true;
         if (lane == 0) {
           if (g >= KS && !mbar_wait_bounded(&emptyb[st], ((g / KS) - 1) & 1, WAIT_LIMIT)) {
@@ -296,15 +398,19 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
           } else if (*abort_flag) {
             fine = false;
           } else {
-            mbar_arrive_expect_tx(&fullb[st], TILE_BYTES);
+            mbar_arrive_expect_tx(&fullb[st], win_tile ? 2u * PAGE * 128u : TILE_BYTES);
           }
         }
         run = __shfl_sync(0xffffffffu, fine, 0);  // also orders expect_tx before the loads
         if (!run) break;
         armed = g + 1;
-        if (boxer)
-          tma_load_4d(gbase + ring + st * TILE_BYTES + my_half * HALF_BYTES + my_pg * PAGE * 128,
-                      tmap, &fullb[st], 0, tok, my_half, I.h, pol_keep);
+        uint8_t* dst = gbase + ring + st * TILE_BYTES + my_half * HALF_BYTES;
+        if (win_tile) {
+          if (lane < 2)
+            tma_load_4d(dst, wmap, &fullb[st], 0, I.q_start, my_half, I.h, pol_once);
+        } else if (boxer) {
+          tma_load_4d(dst + my_pg * PAGE * 128, tmap, &fullb[st], 0, tok, my_half, I.h, pol_keep);
+        }
       }
     }
     // Drain every armed load before the CTA can exit (the ring holds the last
@@ -328,8 +434,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
       bool ok = true;
       uint32_t g = 0;
       int ic = 0;
-      for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++ic) {
-        const Item I = item_at(P, prefix, B, it);
+      for (int k = 0; ok && snake_item(k) < items; ++k, ++ic) {
+        const Item I = item_at(P, prefix, order, B, snake_item(k));
         const int qb = ic & 1;
         if (!is_pv) ok = mbar_wait_bounded(&bar[B_QFULL + qb], (ic >> 1) & 1, WAIT_LIMIT);
         const uint32_t qbase = base + OFF_Q + qb * TILE_BYTES;
@@ -413,11 +519,14 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     };
     uint32_t g = 0;
     int ic = 0;
-    for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++ic) {
-      const Item I = item_at(P, prefix, B, it);
+    for (int k = 0; ok && snake_item(k) < items; ++k, ++ic) {
+      const Item I = item_at(P, prefix, order, B, snake_item(k));
       const int pos = I.pos0 + row / G;  // query position of this row within the sequence
       const int gg = row % G;
-      const int limit = min(I.win_start + pos, I.kv_len - 1);  // last visible key
+      const bool row_valid = row < positions_per_tile(G) * G && pos < I.q_len;
+      // Last visible key: causal over the context; with a window, every pool key
+      // and, in the window tile, window keys 0..pos.
+      const int limit = P.window ? I.pool_len - 1 : min(I.win_start + pos, I.kv_len - 1);
       float m_ref = -INFINITY, l_sum = 0.f;
       for (int j = 0; j < I.nt; ++j, ++g) {
         const int sb = g & 1, pb = g & 1;
@@ -439,7 +548,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         if (lane == 0) mbar_arrive(&bar[B_SFREE + sb]);  // S buffer may be overwritten
 
         // Row max of the raw scores over the visible columns (col0 + c <= limit).
-        const int lim = limit - j * BN - col0;
+        const bool win_tile = P.window && j == I.nt - 1;
+        const int lim = (win_tile ? pos : limit - j * BN) - col0;
         if (__any_sync(0xffffffffu, lim < CW - 1)) {
 #pragma unroll
           for (int c = 0; c < CW; ++c)
@@ -490,11 +600,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
 #pragma unroll
         for (int c = 0; c < CW / 2; ++c) {
           const float x0 = fmaf(sv[2 * c], sl2, nmu), x1 = fmaf(sv[2 * c + 1], sl2, nmu);
-          const float p0 = (POLY_EVERY && (2 * c) % POLY_EVERY == POLY_EVERY - 1) ? exp2_fma(x0)
-                                                                               : fast_exp2(x0);
-          const float p1 = (POLY_EVERY && (2 * c + 1) % POLY_EVERY == POLY_EVERY - 1)
-                               ? exp2_fma(x1)
-                               : fast_exp2(x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
           ps[c & 3] += p0 + p1;
           pk[c] = Mma<T>::pack(p0, p1);
         }
@@ -518,14 +624,18 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         }
         tmem_wait_st();
         const int kbase = j * BN;
-        if (warp == 0 && kbase + BN > I.kv_len) {
-          // Last tile: zero the V rows of keys past the context (whole 128-byte
-          // rows of both halves) so p = 0 adds nothing even where an unwritten
-          // slot holds NaN.  Warp 0's p_full arrival orders it before P V.
+        // Keys of this tile past the last one loaded: past the pool in the last
+        // pool tile, past q_len in the window tile (whose other rows were never
+        // written by this tile's loads).
+        const int loaded = win_tile ? I.q_len : I.pool_len - kbase;
+        if (warp == 0 && loaded < BN) {
+          // Zero the V rows of those keys (whole 128-byte rows of both halves)
+          // so p = 0 adds nothing even where a slot holds NaN.  Warp 0's p_full
+          // arrival orders it before P V.
           const int st = g % KS;
           if (!mbar_wait_bounded(&bar[B_VFULL + st], (g / KS) & 1, WAIT_LIMIT)) ok = false;
           const uint32_t vb = base + OFF_V + st * TILE_BYTES;
-          const int first = max(0, I.kv_len - kbase);
+          const int first = max(0, loaded);
           for (int idx = lane; idx < (BN - first) * 16; idx += 32) {
             const int r = first + idx / 16, c16 = idx % 16;
             const uint32_t a = vb + (c16 >> 3) * HALF_BYTES + r * 128 + (c16 & 7) * 16;
@@ -562,7 +672,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         ok = false;
         break;
       }
-      if (pos < I.q_len) {
+      if (row_valid) {
         const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
         T* orow = static_cast<T*>(P.a.out) + (int64_t)(I.q_start + pos) * P.a.o_sr +
                   (int64_t)(I.h * G + gg) * P.a.o_sh + col0;
@@ -642,8 +752,14 @@ const char* prefill_tc_unsupported(const AttnParams& p, mf_dtype dtype) {
   if ((p.q_sr * 2) % 16 || (p.q_sh * 2) % 16 || (p.o_sr * 2) % 16 || (p.o_sh * 2) % 16)
     return "q/out strides not 16-byte multiples";
   const int G = p.hq / p.hkv;
-  if (G > 8 || pf::BM % G) return "GQA group does not divide 128";
-  if (p.wk || p.row_map) return "window / row_map";
+  if (G < 1 || G > 16) return "GQA group above 16";
+  if (p.row_map) return "row_map";
+  if (p.wk) {
+    if (p.max_q_len > pf::PAGE) return "window longer than 16 rows";
+    if ((p.w_sr * 2) % 16 || (p.w_sh * 2) % 16) return "window strides not 16-byte multiples";
+    if ((reinterpret_cast<uintptr_t>(p.wk) | reinterpret_cast<uintptr_t>(p.wv)) & 15)
+      return "window not 16-byte aligned";
+  }
   if (p.num_seqs > pf::MAX_SEQS) return "more than 4096 sequences";
   if (!p.causal) return "non-causal";
   if ((int64_t)p.num_blocks * pf::PAGE > 0x7fffffffLL) return "pool slots exceed int32";
@@ -655,17 +771,30 @@ int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
   const CUtensorMapDataType dt =
       dtype == MF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int G = p.hq / p.hkv;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mwk, mwv;
   const uint64_t slots = (uint64_t)p.num_blocks * pf::PAGE;
-  // q: (64, heads, halves, rows), box (64, G heads, 1, 128/G positions)
+  const int ppt = pf::positions_per_tile(G);
+  // q: (64, heads, halves, rows), box (64, G heads, 1, floor(128/G) positions)
   CUresult r0 = encode_pf(&mq, p.q, (uint64_t)p.hq, (uint64_t)p.q_sh * 2, (uint64_t)p.total_q,
-                          (uint64_t)p.q_sr * 2, (uint32_t)G, (uint32_t)(pf::BM / G), dt);
+                          (uint64_t)p.q_sr * 2, (uint32_t)G, (uint32_t)ppt, dt);
   // pool: (64, slots, halves, kv heads), box (64, 16 tokens, 1, 1 head)
   CUresult r1 = encode_pf(&mk, p.kp, slots, (uint64_t)p.ss * 2, (uint64_t)p.hkv,
                           (uint64_t)p.sh * 2, pf::PAGE, 1, dt);
   CUresult r2 = encode_pf(&mv, p.vp, slots, (uint64_t)p.ss * 2, (uint64_t)p.hkv,
                           (uint64_t)p.sh * 2, pf::PAGE, 1, dt);
-  if (r0 != CUDA_SUCCESS || r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS)
+  // window: (64, rows, halves, kv heads), box (64, 16 rows, 1, 1 head)
+  CUresult r3 = CUDA_SUCCESS, r4 = CUDA_SUCCESS;
+  if (p.wk) {
+    r3 = encode_pf(&mwk, p.wk, (uint64_t)p.total_q, (uint64_t)p.w_sr * 2, (uint64_t)p.hkv,
+                   (uint64_t)p.w_sh * 2, pf::PAGE, 1, dt);
+    r4 = encode_pf(&mwv, p.wv, (uint64_t)p.total_q, (uint64_t)p.w_sr * 2, (uint64_t)p.hkv,
+                   (uint64_t)p.w_sh * 2, pf::PAGE, 1, dt);
+  } else {
+    mwk = mk;
+    mwv = mv;
+  }
+  if (r0 != CUDA_SUCCESS || r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS || r3 != CUDA_SUCCESS ||
+      r4 != CUDA_SUCCESS)
     return fail(MF_ECUDA, "prefill: tensor map encoding failed");
   pf::Params P;
   P.a = p;
@@ -673,9 +802,10 @@ int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
   P.rows_cap = rows_cap;
   P.scale_log2 = p.scale * 1.4426950408889634f;
   P.in_fmt = dtype == MF_BF16 ? 1u : 0u;
+  P.window = p.wk ? 1 : 0;
   // Persistent grid: one CTA per SM, or fewer when there are fewer items
   // (num_seqs x query tiles of the longest run x kv heads bounds the count).
-  const int64_t q_tiles = ((int64_t)p.max_q_len * G + pf::BM - 1) / pf::BM;
+  const int64_t q_tiles = ((int64_t)p.max_q_len + ppt - 1) / ppt;
   const int64_t items_max = (int64_t)p.num_seqs * q_tiles * p.hkv;
   if (items_max == 0) return MF_OK;
   const int64_t grid = std::min<int64_t>(items_max, current_sm_count());
@@ -691,7 +821,7 @@ int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
     if (e != cudaSuccess) return fail(MF_ECUDA, std::string("prefill: ") + cudaGetErrorString(e));
     configured_dev[which] = dev;
   }
-  kern<<<(unsigned)grid, pf::THREADS, smem, stream>>>(mq, mk, mv, P);
+  kern<<<(unsigned)grid, pf::THREADS, smem, stream>>>(mq, mk, mv, mwk, mwv, P);
   return check_launch("paged attention (tcgen05 prefill)");
 }
 

@@ -98,28 +98,36 @@ static int to_params(const mf_attention_args* a, int32_t* err, AttnParams& p) {
   return MF_OK;
 }
 
-// Decode kernel alone when every query run is short (<= 64 rows per kv head);
-// otherwise the tcgen05 prefill kernel for runs of more than 8 rows plus the
-// decode kernel for the rest (each skips the other's sequences on the device,
-// so the split needs no host knowledge of the lengths); the generic kernel
-// for anything neither serves.
+// Query runs of more than 8 rows per kv head (prefill, speculative verify) go to
+// the tcgen05 kernel when it serves the call, the runs of up to 8 rows of the
+// same call to the decode kernel (each skips the other's sequences on the
+// device, so the split needs no host knowledge of the lengths); when every run
+// fits the decode kernel's other consumers or the tcgen05 kernel does not
+// serve the layout, the decode kernel alone; the generic kernel for anything
+// neither serves.
 Dispatch plan_dispatch(const AttnParams& p, mf_dtype dtype, int sm_count) {
   Dispatch d;
   const bool window = p.wk != nullptr;
+  const int G = p.hq / p.hkv;
+  if ((int64_t)G * p.max_q_len > 8 && prefill_tc_unsupported(p, dtype) == nullptr) {
+    if (G > 8) {
+      d.mode = Dispatch::PREFILL;  // no run is short enough for the decode kernel
+      d.rows_cap = 0;
+      return d;
+    }
+    d.short_p = p;
+    d.short_p.max_q_len = 8 / G;
+    d.decode = plan_attn_tc(d.short_p, dtype, sm_count, window, true);
+    if (d.decode.ok && d.decode.SW) {
+      d.mode = Dispatch::MIXED;
+      d.rows_cap = d.decode.rows_cap;
+      return d;
+    }
+  }
   d.decode = plan_attn_tc(p, dtype, sm_count, window);
   if (d.decode.ok) {
     d.mode = Dispatch::DECODE;
     return d;
-  }
-  const int G = p.hq / p.hkv;
-  if (!window && G <= 8 && prefill_tc_unsupported(p, dtype) == nullptr) {
-    d.short_p = p;
-    d.short_p.max_q_len = 8 / G;
-    d.decode = plan_attn_tc(d.short_p, dtype, sm_count, false, true);
-    if (d.decode.ok && d.decode.SW) {
-      d.mode = Dispatch::MIXED;
-      return d;
-    }
   }
   d.mode = Dispatch::GENERIC;
   return d;
@@ -146,7 +154,7 @@ extern "C" size_t mf_paged_attention_workspace_size(const mf_attention_args* arg
   AttnParams p{};
   if (to_params(args, nullptr, p) != MF_OK) return 0;
   const Dispatch d = plan_dispatch(p, args->dtype, sm_count_of(device));
-  return d.mode == Dispatch::GENERIC ? 0 : d.decode.ws_bytes;
+  return (d.mode == Dispatch::DECODE || d.mode == Dispatch::MIXED) ? d.decode.ws_bytes : 0;
 }
 
 extern "C" int mf_paged_attention(const mf_attention_args* args, void* workspace,
@@ -158,11 +166,12 @@ extern "C" int mf_paged_attention(const mf_attention_args* args, void* workspace
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Dispatch d = plan_dispatch(p, args->dtype, current_sm_count());
   if (d.mode == Dispatch::GENERIC) return launch_attn_generic(p, args->dtype, s);
+  if (d.mode == Dispatch::PREFILL) return launch_attn_prefill_tc(p, args->dtype, 0, s);
   if (!workspace || workspace_bytes < d.decode.ws_bytes)
     return fail(MF_EWORKSPACE, "paged attention: workspace missing or smaller than "
                                "mf_paged_attention_workspace_size()");
   if (d.mode == Dispatch::DECODE) return launch_attn_tc(p, args->dtype, d.decode, workspace, s);
-  rc = launch_attn_prefill_tc(p, args->dtype, d.decode.rows_cap, s);
+  rc = launch_attn_prefill_tc(p, args->dtype, d.rows_cap, s);
   if (rc != MF_OK) return rc;
   return launch_attn_tc(d.short_p, args->dtype, d.decode, workspace, s);
 }

@@ -74,9 +74,13 @@ int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
 
 // How one mf_paged_attention call is split across kernels.
 struct Dispatch {
-  enum Mode { DECODE, MIXED, GENERIC } mode = GENERIC;
-  TcPlan decode;      // DECODE / MIXED: the decode kernel's plan
+  // DECODE: decode kernel alone.  MIXED: tcgen05 kernel for runs of more than
+  // rows_cap rows per kv head, decode kernel for the rest.  PREFILL: tcgen05
+  // kernel alone (every run is long).  GENERIC: CUDA-core kernel.
+  enum Mode { DECODE, MIXED, PREFILL, GENERIC } mode = GENERIC;
+  TcPlan decode;       // DECODE / MIXED: the decode kernel's plan
   AttnParams short_p;  // MIXED: the decode kernel's view (short runs only)
+  int rows_cap = 0;    // MIXED / PREFILL: longest run the decode kernel keeps
 };
 Dispatch plan_dispatch(const AttnParams& p, mf_dtype dtype, int sm_count);
 int launch_attn_tc(const AttnParams& p, mf_dtype dtype, const TcPlan& plan, void* ws,

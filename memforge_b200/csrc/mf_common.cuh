@@ -192,23 +192,6 @@ MF_DEVINL float fast_exp2(float x) {
   return y;
 }
 
-// 2^x for x <= 8 on the FMA pipe, to share the exponentials of a softmax tile
-// with the SFU.  Range reduction: adding 1.5 * 2^23 rounds x to the nearest
-// integer n (held in the low mantissa bits of t), f = x - n lies in [-1/2, 1/2];
-// 2^f is a degree-3 polynomial whose coefficients were fitted here for minimum
-// relative error on [-1/2, 1/2] (iteratively reweighted least squares; max
-// relative error 7.5e-5, far below 16-bit rounding); n is added to the
-// exponent field as an integer.  Inputs below -126 give 2^-126 or less.
-MF_DEVINL float exp2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  float p = fmaf(0.05517149344086647f, f, 0.24261093139648438f);
-  p = fmaf(p, f, 0.6932609677314758f);
-  p = fmaf(p, f, 0.9999280571937561f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 }  // namespace mf
 
 // ------------------------------------------------------- tcgen05 / TMEM (sm_100a)

@@ -91,6 +91,29 @@ def test_verify_window_matches_oracle(hq, hkv, W):
     check(c, window)
 
 
+def test_verify_window_ignores_stale_pool_slots():
+    """With a side window the pool holds only the context: NaN in its unwritten
+    slots (where the window's positions would go) must not leak."""
+    W = 5
+    c = cases.small_decode_case("wstale", 19, "bf16", 40, 8, 128, [W + 37, W + 128, W + 300],
+                                q_per_seq=W)
+    g = cases.rng(19)
+    window = {s: (int(c.ctx_lens[s]) - W, cases.bf16_round(cases.normal(g, (8, W, 128))),
+                  cases.bf16_round(cases.normal(g, (8, W, 128)))) for s in range(c.batch)}
+    a = run_case(c, window)
+    for s in range(c.batch):
+        n = int(c.ctx_lens[s]) - W  # pool positions 0 .. n-1 are written
+        for pos in range(n, n + W):
+            blk = c.tables[s][pos // 16]
+            if blk >= 0:
+                c.k_pool[blk, pos % 16] = np.nan
+                c.v_pool[blk, pos % 16] = np.nan
+    b = run_case(c, window)
+    assert np.isfinite(b).all()
+    assert np.array_equal(a, b)
+    check(c, window)
+
+
 @pytest.mark.parametrize("W", [2, 5, 16])
 def test_multi_row_causal_from_pool(W):
     """Verify-style rows whose keys are already in the pool (no side window)."""

@@ -93,9 +93,18 @@ def test_prefill_mixed_with_decodes_in_one_call():
     check(varlen_case(5, "bf16", 32, 8, 128, runs), "mixed")
 
 
-@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (64, 8), (8, 1)])
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (64, 8), (8, 1), (40, 8), (48, 8), (56, 8),
+                                     (64, 4)])
 def test_gqa_groups(hq, hkv):
     check(varlen_case(6, "bf16", hq, hkv, 128, [(150, 400), (77, 77)]), f"gqa {hq}/{hkv}")
+
+
+def test_many_sequences_in_the_sorted_work_list():
+    """300 short runs of varied length: the kernel sorts its work list by kv_len
+    (longest first) across more sequences than it has threads."""
+    g = np.random.default_rng(8)
+    runs = [(int(q), int(q + g.integers(0, 300))) for q in g.integers(3, 40, size=300)]
+    check(varlen_case(8, "bf16", 32, 8, 128, runs), "300 runs")
 
 
 def test_fp16():
