@@ -56,6 +56,9 @@ def measured_peaks():
 
 # ------------------------------------------------------------------ workload
 
+MODEL_OF = {"cfg2": "Llama-3-8B", "cfg5": "Llama-3-70B", "cfg4": "Qwen2.5-14B"}
+
+
 def workload(name: str, world: int):
     """Host-side metadata of the benchmark workload (identical on every rank)."""
     from tests import cases
@@ -316,8 +319,9 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded; random-init pool)",
-            "config": {"workload": f"BASELINE {w['name']}: KV write + decode, Llama-3-8B attention "
-                                   f"(Hq 32, Hkv 8, D 128), block 16",
+            "config": {"workload": f"BASELINE {w['name']}: KV write + decode, "
+                                   f"{MODEL_OF.get(w['name'], '')} attention "
+                                   f"(Hq {w['Hq']}, Hkv {w['Hkv']}, D {w['D']}), block 16",
                        "batch": B, "kv_heads_per_gpu": hkv, "sum_ctx": int(w["ctx"].sum()),
                        "pool_blocks": NB, "parallelism": f"kv-head shard x{world}" if world > 1 else "1 GPU",
                        "l2": "inputs exceed L2 (KV read per step > 126 MB); no flush",
