@@ -237,35 +237,54 @@ def run_ours(args):
     slots_np = (w["tables"][np.arange(B), pos // BLOCK].astype(np.int64) * BLOCK + pos % BLOCK)
     slots = torch.from_numpy(slots_np.astype(np.int32)).to(dev)
     out = torch.empty((B * W, hq, D), device=dev, dtype=torch.bfloat16)
-    staging = torch.empty((world * B * W, hq, D), device=dev, dtype=torch.bfloat16) if world > 1 else None
-    full_out = torch.empty((B * W, hq * world, D), device=dev, dtype=torch.bfloat16) if world > 1 else None
     scale = 1.0 / math.sqrt(D)
+    # N > 1: the full [B, Hq, D] output is assembled over peer memory: every
+    # rank's decode kernel stores its heads into all ranks' output buffers
+    # (two, alternating per step) and a flag barrier completes the step.
+    peer = None
+    if world > 1:
+        from memforge_b200.kv_shard import PeerOutput
+        peer = PeerOutput(B * W, hq * world, D, torch.bfloat16, dev)
 
     def write():
         K.reshape_and_cache(new_k, new_v, kp, vp, slots)
 
-    def attend():
-        K.paged_attention(q, out, kp, vp, tables, ctx, q_per_seq=1, scale=scale, causal=True)
+    def attend(buf=None):
+        if peer is None:
+            K.paged_attention(q, out, kp, vp, tables, ctx, q_per_seq=1, scale=scale, causal=True)
+        else:
+            K.paged_attention(q, peer.outs[buf], kp, vp, tables, ctx, q_per_seq=1, scale=scale,
+                              causal=True, out_peers=peer.pointers(buf),
+                              out_head_offset=rank * hq)
 
     def collective():
-        if world > 1:
-            from memforge_b200.kv_shard import gather_heads
-            gather_heads(out, out=full_out, staging=staging)
+        if peer is not None:
+            peer.barrier()
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(3, args.warmup)):
         write()
-        attend()
+        attend(None if peer is None else peer.current)
         collective()
     torch.cuda.synchronize(dev)
     K.check_device_errors(dev)
     # Each kernel is captured once in a CUDA graph and replayed every step (the
     # way MemForge's graphed decode runs), so host launch cost stays off the
-    # device timeline; events between the replays time each kernel.
-    (g_write, n_write), (g_attn, n_attn) = capture_graph(write, dev), capture_graph(attend, dev)
+    # device timeline; events between the replays time each kernel.  With peer
+    # output there is one attention graph per output buffer.
+    g_write, n_write = capture_graph(write, dev)
+    if peer is None:
+        g_attns = [capture_graph(attend, dev)]
+    else:
+        g_attns = [capture_graph(lambda b=b: attend(b), dev) for b in range(len(peer.outs))]
+    n_attn = g_attns[0][1]
+
+    def g_attn_replay():
+        g_attns[0 if peer is None else peer.current][0].replay()
+
     for _ in range(max(3, args.warmup)):
         g_write.replay()
-        g_attn.replay()
+        g_attn_replay()
         collective()
     torch.cuda.synchronize(dev)
     K.check_device_errors(dev)
@@ -284,7 +303,7 @@ def run_ours(args):
             a.record(stream)
             g_write.replay()
             b.record(stream)
-            g_attn.replay()
+            g_attn_replay()
             c.record(stream)
             collective()
         end_all.record(stream)
@@ -294,7 +313,7 @@ def run_ours(args):
     total_ms = start_all.elapsed_time(end_all)
     decode_ms = [b.elapsed_time(c) for a, b, c in ev]
     write_ms = [a.elapsed_time(b) for a, b, c in ev]
-    kernel_launches = (n_write + n_attn) * args.steps
+    kernel_launches = (n_write + n_attn + (1 if peer is not None else 0)) * args.steps
     K.check_device_errors(dev)
 
     t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
@@ -309,7 +328,7 @@ def run_ours(args):
     achieved = attn_b / (dec_ms * 1e-3) / 1e9
 
     # ------------------------------------------------ end-to-end (host buffers)
-    e2e = run_e2e(args, w, dev, kp, vp, hkv, hq, world)
+    e2e = run_e2e(args, w, dev, kp, vp, hkv, hq, world, peer, rank)
 
     res = None
     if rank == 0:
@@ -344,6 +363,8 @@ def run_ours(args):
                                    "sample": sample}
         print(json.dumps(res), flush=True)
     if world > 1:
+        del g_attns
+        peer.close()
         dist.barrier()
         dist.destroy_process_group()
     return res
@@ -372,14 +393,16 @@ def capture_graph(fn, dev):
     return g, sum(K.launch_counter.values()) - before
 
 
-def run_e2e(args, w, dev, kp, vp, hkv, hq, world):
+def run_e2e(args, w, dev, kp, vp, hkv, hq, world, peer=None, rank=0):
     """
     Same step through the reference-facing API with HOST inputs: every step
     copies q, new K/V, slot map, block tables and lengths from pinned host
-    memory, runs scatter_kv + paged_decode_attention (at N > 1 also the NCCL
-    all-gather of the heads), and reads the output back to pinned host memory.
-    The device part of the step is one CUDA graph (copies and kernels), as in
-    MemForge's graphed decode; the all-gather and the read-back follow it.
+    memory, runs scatter_kv + paged_decode_attention, and reads the output back
+    to pinned host memory.  The device part of the step is one CUDA graph
+    (copies and kernels), as in MemForge's graphed decode.  At N > 1 the
+    attention stores its heads into every rank's output over peer memory
+    (kv_shard.PeerOutput, one graph per output buffer), the peer barrier
+    completes the step and the full output is read back.
     """
     import torch
     from memforge_b200.paged_decode import paged_decode_attention
@@ -399,25 +422,24 @@ def run_e2e(args, w, dev, kp, vp, hkv, hq, world):
     stream = torch.cuda.current_stream(dev)
     d_in = [torch.empty_like(t, device=dev) for t in (h_q, h_k, h_v, h_slots, h_tab, h_ctx)]
     res = {}
-    if world > 1:
-        from memforge_b200.kv_shard import gather_heads
-        staging = torch.empty((world * B, hq, D), device=dev, dtype=torch.bfloat16)
-        full = torch.empty((B, hq * world, D), device=dev, dtype=torch.bfloat16)
 
-    def device_part():
+    def device_part(buf=None):
         for d, h in zip(d_in, (h_q, h_k, h_v, h_slots, h_tab, h_ctx)):
             d.copy_(h, non_blocking=True)
         q, k, v, sl, tab, cx = d_in
         K.reshape_and_cache(k, v, kp, vp, sl)
-        res["o"] = paged_decode_attention(q, kp.view(-1, hkv, D), vp.view(-1, hkv, D), tab, cx,
-                                          BLOCK, int(w["ctx"].max()), scale)
         if world == 1:
+            res["o"] = paged_decode_attention(q, kp.view(-1, hkv, D), vp.view(-1, hkv, D), tab,
+                                              cx, BLOCK, int(w["ctx"].max()), scale)
             h_out.copy_(res["o"], non_blocking=True)
+        else:
+            K.paged_attention(q, peer.outs[buf], kp, vp, tab, cx, q_per_seq=1, scale=scale,
+                              causal=True, out_peers=peer.pointers(buf),
+                              out_head_offset=rank * hq)
 
     def tail():
         if world > 1:
-            gather_heads(res["o"], out=full, staging=staging)
-            h_out.copy_(full, non_blocking=True)
+            h_out.copy_(peer.barrier(), non_blocking=True)
 
     def timed(step):
         for _ in range(3):
@@ -435,9 +457,15 @@ def run_e2e(args, w, dev, kp, vp, hkv, hq, world):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    eager_ms = timed(lambda: (device_part(), tail()))
-    g, _ = capture_graph(device_part, dev)
-    ms = timed(lambda: (g.replay(), tail()))
+    if world == 1:
+        eager_ms = timed(lambda: (device_part(), tail()))
+        g, _ = capture_graph(device_part, dev)
+        ms = timed(lambda: (g.replay(), tail()))
+    else:
+        eager_ms = timed(lambda: (device_part(peer.current), tail()))
+        gs = [capture_graph(lambda b=b: device_part(b), dev)[0] for b in range(len(peer.outs))]
+        ms = timed(lambda: (gs[peer.current].replay(), tail()))
+        g = gs
     attn_b, write_b = algorithmic_bytes(w, hkv, hq)
     bi = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_tab, h_ctx))
     bo = h_out.numel() * h_out.element_size()
@@ -446,9 +474,12 @@ def run_e2e(args, w, dev, kp, vp, hkv, hq, world):
             "ms_per_step": round(ms, 5), "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
             "eager_value": round((attn_b + write_b) * world / (eager_ms * 1e-3) / 1e9, 2),
             "eager_ms_per_step": round(eager_ms, 5),
-            "api": "memforge_b200 reshape_and_cache + paged_decode_attention, pinned host "
-                   "buffers; H2D copies + kernels + D2H replayed as one CUDA graph"
-                   + (" + NCCL all-gather of heads" if world > 1 else "")}
+            "api": ("memforge_b200 reshape_and_cache + paged_decode_attention, pinned host "
+                    "buffers; H2D copies + kernels + D2H replayed as one CUDA graph")
+                   if world == 1 else
+                   ("memforge_b200 reshape_and_cache + paged attention storing its heads into "
+                    "every rank's output (kv_shard.PeerOutput) + peer barrier, pinned host "
+                    "buffers; H2D copies + kernels replayed as CUDA graphs, full output read back")}
 
 
 # ----------------------------------------------------------- reference arm

@@ -116,8 +116,11 @@ MF_API int mf_reshape_and_cache(const void* key, const void* value, mf_dtype src
  * row_map (optional) sends logical row r to packed row row_map[r] for q, out
  * and the window (arbitrary packing orders, varlen_attention.py:60-75).
  */
+#define MF_MAX_OUT_PEERS 8
+
 typedef struct {
-  uint32_t struct_size; /* sizeof(mf_attention_args) */
+  uint32_t struct_size; /* sizeof(mf_attention_args); the size up to `dtype` is
+                           accepted too (no peer output) */
   const void* q;        /* [rows][num_q_heads][head_dim] */
   int64_t q_stride_row, q_stride_head;
   void* out;            /* same indexing as q */
@@ -140,6 +143,22 @@ typedef struct {
   float scale;
   int32_t causal;
   mf_dtype dtype;
+  /* Head-sharded output over peer memory (optional; read only when struct_size
+   * is the full size of this struct, and ignored when num_out_peers == 0).
+   * When a KV pool is split by kv head across GPUs (one process per GPU, the
+   * partition memforge_b200.kv_shard implements), each GPU computes
+   * num_q_heads heads of a wider output [rows][total heads][head_dim].  With
+   * num_out_peers = N > 0 the decode kernel writes every output row of its
+   * heads, at head index out_head_offset + local head, straight into all N
+   * buffers out_peers[0..N-1] (this GPU's own and the peers' copies of that
+   * output, mapped into this process, e.g. through CUDA IPC), with the
+   * out_stride_* strides; `out` is not written.  This replaces the all-gather
+   * after the attention with stores over NVLink.  The peers may read the output
+   * once mf_peer_barrier has completed on every GPU.  Decode batches only (every
+   * run of up to 8 rows per kv head): other batches return MF_EUNSUPPORTED. */
+  int32_t num_out_peers;
+  int32_t out_head_offset;
+  void* out_peers[MF_MAX_OUT_PEERS];
 } mf_attention_args;
 
 /* Device workspace `mf_paged_attention` needs for these arguments on `device`
@@ -187,6 +206,36 @@ MF_API int mf_paged_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h
  * Arguments and semantics are those of mf_paged_decode.
  */
 #define MF_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/*
+ * mf_peer_barrier — completes a head-sharded step (see num_out_peers above).
+ *
+ * No single counterpart in the reference: it takes the place of the NCCL
+ * all-gather of head slices that follows sharded attention.  flags[p] is
+ * process-mapped memory of GPU p holding `world` int32 counters (zero-filled
+ * once).  Stream-ordered after this GPU's attention launch, it publishes `epoch`
+ * into every GPU's counter for this rank (system-scope release stores over
+ * NVLink) and waits until this GPU's counters from all ranks reach `epoch`
+ * (acquire loads).  `epoch` must increase by one per step, starting at 1.  The
+ * wait is bounded (2 s): on expiry it sets MF_ERR_TIMEOUT in err_flag and
+ * returns, leaving the context usable.
+ */
+MF_API int mf_peer_barrier(int32_t* const* flags, int32_t world, int32_t rank, uint32_t epoch,
+                           int32_t* err_flag, mf_stream_t stream);
+
+/*
+ * CUDA IPC for the peer buffers of a head-sharded step (no counterpart in the
+ * reference, which is single-GPU).  mf_ipc_export gives the 64-byte IPC handle
+ * of the allocation holding device address `ptr` and ptr's offset in it;
+ * mf_ipc_open, in another process of the same node with its own device
+ * current, maps that allocation (enabling peer access) and returns the address
+ * of the exported byte; mf_ipc_close unmaps it.  One allocation can be opened
+ * once per process.
+ */
+#define MF_IPC_HANDLE_BYTES 64
+MF_API int mf_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+MF_API int mf_ipc_open(const void* handle, uint64_t offset, void** ptr);
+MF_API int mf_ipc_close(void* ptr, uint64_t offset);
 
 MF_API int mf_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                                    const void* key_flat, const void* value_flat,

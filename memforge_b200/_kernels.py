@@ -22,7 +22,7 @@ from __future__ import annotations
 
 import os
 import threading
-from typing import Dict, Optional
+from typing import Dict, Optional, Sequence
 
 import torch
 
@@ -34,7 +34,8 @@ _state_lock = threading.Lock()
 _workspaces: Dict[int, torch.Tensor] = {}
 _err_words: Dict[int, torch.Tensor] = {}
 _checks = os.environ.get("MEMFORGE_CHECK", "0") not in ("", "0")
-launch_counter = {"reshape_and_cache": 0, "paged_attention": 0, "copy_blocks": 0}
+launch_counter = {"reshape_and_cache": 0, "paged_attention": 0, "copy_blocks": 0,
+                  "peer_barrier": 0}
 
 
 def set_checks(enabled: bool) -> None:
@@ -195,7 +196,8 @@ def paged_attention(q: torch.Tensor, out: torch.Tensor, key_pool: torch.Tensor,
                     q_per_seq: int = 1, max_q_len: Optional[int] = None, scale: float,
                     causal: bool = True, row_map: Optional[torch.Tensor] = None,
                     win_k: Optional[torch.Tensor] = None, win_v: Optional[torch.Tensor] = None,
-                    heads_major: bool = False, workspace_tensor: Optional[torch.Tensor] = None
+                    heads_major: bool = False, workspace_tensor: Optional[torch.Tensor] = None,
+                    out_peers: Optional[Sequence[int]] = None, out_head_offset: int = 0
                     ) -> torch.Tensor:
     """
     ``mf_paged_attention`` on torch tensors.
@@ -206,6 +208,9 @@ def paged_attention(q: torch.Tensor, out: torch.Tensor, key_pool: torch.Tensor,
     block_tables: int32 ``[num_seqs, width]``; kv_lens: int32 ``[num_seqs]``;
     cu_seqlens_q: int32 ``[num_seqs+1]`` or None (uniform ``q_per_seq``);
     row_map: int32 ``[rows]`` or None; win_k/win_v: ``(rows, Hkv, D)`` or None.
+    out_peers: device addresses of the full ``[rows, total heads, D]`` output on
+    every GPU of a head-sharded step (``out`` gives their strides); the kernel
+    stores this call's heads at ``out_head_offset`` into all of them.
     """
     require_cuda("paged_attention", q, out, key_pool, value_pool, block_tables, kv_lens,
                  cu_seqlens_q, row_map, win_k, win_v)
@@ -253,6 +258,12 @@ def paged_attention(q: torch.Tensor, out: torch.Tensor, key_pool: torch.Tensor,
     a.max_q_len = max_q_len if max_q_len is not None else q_per_seq
     a.num_q_heads, a.num_kv_heads, a.head_dim = hq, hkv, d
     a.scale, a.causal, a.dtype = float(scale), 1 if causal else 0, dtype_code(q.dtype)
+    if out_peers:
+        if len(out_peers) > L.MF_MAX_OUT_PEERS:
+            raise ValueError(f"at most {L.MF_MAX_OUT_PEERS} output peers")
+        a.num_out_peers, a.out_head_offset = len(out_peers), int(out_head_offset)
+        for i, ptr in enumerate(out_peers):
+            a.out_peers[i] = int(ptr)
     lib = L.lib()
     dev = q.device
     idx = _dev_index(q)
@@ -276,3 +287,14 @@ def ctypes_sizeof_args() -> int:
         import ctypes
         _ARGS_SIZE = ctypes.sizeof(L.AttentionArgs)
     return _ARGS_SIZE
+
+
+def peer_barrier(flag_ptrs: Sequence[int], rank: int, epoch: int,
+                 device: torch.device) -> None:
+    """``mf_peer_barrier``: completes a head-sharded step (see ``kv_shard.PeerOutput``)."""
+    import ctypes
+    arr = (ctypes.c_void_p * len(flag_ptrs))(*[int(p) for p in flag_ptrs])
+    rc = L.lib().mf_peer_barrier(arr, len(flag_ptrs), int(rank), int(epoch),
+                                 err_word(device).data_ptr(), _stream_ptr(device))
+    L.check(rc, "mf_peer_barrier")
+    launch_counter["peer_barrier"] += 1

@@ -43,8 +43,13 @@ ERR_NAMES = {
 EXPORTED = (
     "mf_abi_version", "mf_last_error", "mf_device_info", "mf_reshape_and_cache",
     "mf_paged_attention_workspace_size", "mf_paged_attention", "mf_paged_decode",
-    "mf_copy_blocks", "mf_paged_decode_noalloc",
+    "mf_copy_blocks", "mf_paged_decode_noalloc", "mf_peer_barrier", "mf_ipc_export",
+    "mf_ipc_open", "mf_ipc_close",
 )
+
+MF_IPC_HANDLE_BYTES = 64
+
+MF_MAX_OUT_PEERS = 8
 
 c_i32, c_i64, c_f32, c_vp, c_sz = (ctypes.c_int32, ctypes.c_int64, ctypes.c_float,
                                    ctypes.c_void_p, ctypes.c_size_t)
@@ -66,6 +71,8 @@ class AttentionArgs(ctypes.Structure):
         ("num_seqs", c_i32), ("total_q", c_i32), ("max_q_len", c_i32),
         ("num_q_heads", c_i32), ("num_kv_heads", c_i32), ("head_dim", c_i32),
         ("scale", c_f32), ("causal", c_i32), ("dtype", ctypes.c_int),
+        ("num_out_peers", c_i32), ("out_head_offset", c_i32),
+        ("out_peers", c_vp * MF_MAX_OUT_PEERS),
     ]
 
 
@@ -96,6 +103,11 @@ def _declare(lib):
         c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_i32, c_vp, c_i32,
         c_i32, c_i32, c_i32, c_i32, c_f32, ctypes.c_int, c_vp, c_vp, c_sz, c_vp, c_vp]
     lib.mf_copy_blocks.argtypes = [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp, c_vp]
+    lib.mf_peer_barrier.argtypes = [ctypes.POINTER(c_vp), c_i32, c_i32, ctypes.c_uint32, c_vp,
+                                     c_vp]
+    lib.mf_ipc_export.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]
+    lib.mf_ipc_open.argtypes = [c_vp, ctypes.c_uint64, ctypes.POINTER(c_vp)]
+    lib.mf_ipc_close.argtypes = [c_vp, ctypes.c_uint64]
     lib.mf_paged_decode_noalloc.argtypes = [
         c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_i32, c_vp, c_i32,
         c_i32, c_i32, c_i32, c_i32, c_f32, ctypes.c_int, c_vp, c_vp, c_vp]

@@ -312,7 +312,6 @@ MF_DEVINL void merge_rows(const Ctx& C, const PartLayout<RU, DU>& PL, int hg, in
       }
     }
   }
-  T* obase = static_cast<T*>(P.a.out);
 #pragma unroll
   for (int i = 0; i < NR; ++i) {
     const int r = i * RPL + lr;
@@ -320,12 +319,17 @@ MF_DEVINL void merge_rows(const Ctx& C, const PartLayout<RU, DU>& PL, int hg, in
     if (r >= rows) continue;
     const int qi = (row0 + r) / P.G, gg = (row0 + r) % P.G;
     const float inv = Lr > 0.f ? 1.f / Lr : 0.f;
-    T* orow = obase + (int64_t)map_row(P.a, q_start + qi) * P.a.o_sr +
-              (int64_t)(head * P.G + gg) * P.a.o_sh + col0 + lc;
-    orow[0] = from_f32<T>(acc[i].x * inv);
-    orow[1] = from_f32<T>(acc[i].y * inv);
-    orow[2] = from_f32<T>(acc[i].z * inv);
-    orow[3] = from_f32<T>(acc[i].w * inv);
+    const int64_t off = (int64_t)map_row(P.a, q_start + qi) * P.a.o_sr +
+                        (int64_t)(head * P.G + gg) * P.a.o_sh + col0 + lc;
+    const T v0 = from_f32<T>(acc[i].x * inv), v1 = from_f32<T>(acc[i].y * inv);
+    const T v2 = from_f32<T>(acc[i].z * inv), v3 = from_f32<T>(acc[i].w * inv);
+    for (int t = 0; t < out_targets(P.a); ++t) {
+      T* orow = out_at<T>(P.a, t, off);
+      orow[0] = v0;
+      orow[1] = v1;
+      orow[2] = v2;
+      orow[3] = v3;
+    }
   }
 }
 
@@ -399,7 +403,6 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
   const int64_t lo = C.S.bound(vc);
   const int len = C.S.len(vc);
   const T* qbase = static_cast<const T*>(P.a.q);
-  T* obase = static_cast<T*>(P.a.out);
   const float sl2 = P.scale_log2;
   const int NS = P.NS, G = P.G, causal = P.a.causal, window = P.window;
   const uint32_t stage_bytes = C.L.stage_bytes, page_bytes = C.L.page_bytes;
@@ -544,12 +547,15 @@ MF_DEVINL void consume_swapped(const Ctx& C) {
         const int qi = r / P.G, gg = r % P.G;
         if (qi >= geo.q_len) continue;
         const float inv = lrow[j] > 0.f ? 1.f / lrow[j] : 0.f;
-        T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
-                  (int64_t)(head * P.G + gg) * P.a.o_sh;
+        const int64_t off = (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
+                            (int64_t)(head * P.G + gg) * P.a.o_sh;
+        for (int t = 0; t < out_targets(P.a); ++t) {
+          T* orow = out_at<T>(P.a, t, off);
 #pragma unroll
-        for (int n = 0; n < D / 16; ++n) {
-          orow[n * 16 + g4] = from_f32<T>(o[n][j] * inv);
-          orow[n * 16 + 8 + g4] = from_f32<T>(o[n][2 + j] * inv);
+          for (int n = 0; n < D / 16; ++n) {
+            orow[n * 16 + g4] = from_f32<T>(o[n][j] * inv);
+            orow[n * 16 + 8 + g4] = from_f32<T>(o[n][2 + j] * inv);
+          }
         }
       }
       first_piece = false;
@@ -615,7 +621,6 @@ MF_DEVINL void consume_split(const Ctx& C) {
   const int64_t lo = C.S.bound(vc);
   const int len = C.S.len(vc);
   const T* qbase = static_cast<const T*>(P.a.q);
-  T* obase = static_cast<T*>(P.a.out);
   const float sl2 = P.scale_log2;
   const PartLayout<RU, DH> PL{P, units * RU};
 
@@ -761,12 +766,15 @@ MF_DEVINL void consume_split(const Ctx& C) {
         const int qi = r / P.G, gg = r % P.G;
         if (qi >= geo.q_len) continue;
         const float inv = lrow[h2] > 0.f ? 1.f / lrow[h2] : 0.f;
-        T* orow = obase + (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
-                  (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
+        const int64_t off = (int64_t)map_row(P.a, geo.q_start + qi) * P.a.o_sr +
+                            (int64_t)(head * P.G + gg) * P.a.o_sh + dh * DH;
+        for (int t = 0; t < out_targets(P.a); ++t) {
+          T* orow = out_at<T>(P.a, t, off);
 #pragma unroll
-        for (int n = 0; n < DH / 8; ++n) {
-          *reinterpret_cast<uint32_t*>(orow + n * 8 + 2 * c4) =
-              M::pack(o[n][2 * h2] * inv, o[n][2 * h2 + 1] * inv);
+          for (int n = 0; n < DH / 8; ++n) {
+            *reinterpret_cast<uint32_t*>(orow + n * 8 + 2 * c4) =
+                M::pack(o[n][2 * h2] * inv, o[n][2 * h2 + 1] * inv);
+          }
         }
       }
       first_piece = false;

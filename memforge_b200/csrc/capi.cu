@@ -42,10 +42,32 @@ static int sm_count_of(int device) {
   return n;
 }
 
+// sizeof(mf_attention_args) before the peer-output fields were added.
+constexpr uint32_t kArgsSizeNoPeers =
+    (uint32_t)((offsetof(mf_attention_args, num_out_peers) + alignof(mf_attention_args) - 1) /
+               alignof(mf_attention_args) * alignof(mf_attention_args));
+
 static int to_params(const mf_attention_args* a, int32_t* err, AttnParams& p) {
   if (!a) return fail(MF_EINVAL, "paged attention: null args");
-  if (a->struct_size != sizeof(mf_attention_args))
+  // The size up to `dtype` (callers built before the peer-output fields) is
+  // accepted and means no peer output.
+  const bool full = a->struct_size == sizeof(mf_attention_args);
+  if (!full && a->struct_size != kArgsSizeNoPeers)
     return fail(MF_EINVAL, "paged attention: mf_attention_args size mismatch (ABI version)");
+  p.n_peers = 0;
+  p.out_head_offset = 0;
+  if (full && a->num_out_peers != 0) {
+    if (a->num_out_peers < 0 || a->num_out_peers > MF_MAX_OUT_PEERS)
+      return fail(MF_EINVAL, "paged attention: num_out_peers outside [0, MF_MAX_OUT_PEERS]");
+    if (a->out_head_offset < 0)
+      return fail(MF_EINVAL, "paged attention: negative out_head_offset");
+    for (int i = 0; i < a->num_out_peers; ++i) {
+      if (!a->out_peers[i]) return fail(MF_EINVAL, "paged attention: null out_peers entry");
+      p.out_peers[i] = a->out_peers[i];
+    }
+    p.n_peers = a->num_out_peers;
+    p.out_head_offset = a->out_head_offset;
+  }
   if (a->num_seqs < 0 || a->total_q < 0 || a->max_q_len < 0)
     return fail(MF_EINVAL, "paged attention: negative size");
   if (a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->head_dim <= 0)
@@ -60,8 +82,8 @@ static int to_params(const mf_attention_args* a, int32_t* err, AttnParams& p) {
     return fail(MF_EINVAL, "paged attention: q_per_seq must be positive without cu_seqlens_q");
   if ((a->win_k == nullptr) != (a->win_v == nullptr))
     return fail(MF_EINVAL, "paged attention: win_k and win_v go together");
-  if (a->num_seqs > 0 && (!a->q || !a->out || !a->k_pool || !a->v_pool || !a->block_tables ||
-                          !a->kv_lens))
+  if (a->num_seqs > 0 && (!a->q || (!a->out && p.n_peers == 0) || !a->k_pool || !a->v_pool ||
+                          !a->block_tables || !a->kv_lens))
     return fail(MF_EINVAL, "paged attention: null pointer");
   p.q = a->q;
   p.q_sr = a->q_stride_row;
@@ -165,6 +187,9 @@ extern "C" int mf_paged_attention(const mf_attention_args* args, void* workspace
   if (p.num_seqs == 0 || p.total_q == 0) return MF_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const Dispatch d = plan_dispatch(p, args->dtype, current_sm_count());
+  if (p.n_peers > 0 && d.mode != Dispatch::DECODE)
+    return fail(MF_EUNSUPPORTED, "paged attention: peer output (num_out_peers) is served for "
+                                 "decode batches only");
   if (d.mode == Dispatch::GENERIC) return launch_attn_generic(p, args->dtype, s);
   if (d.mode == Dispatch::PREFILL) return launch_attn_prefill_tc(p, args->dtype, 0, s);
   if (!workspace || workspace_bytes < d.decode.ws_bytes)

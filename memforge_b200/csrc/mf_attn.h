@@ -29,7 +29,22 @@ struct AttnParams {
   float scale;
   int32_t causal;
   int32_t* err;
+  // Head-sharded output: when n_peers > 0, output rows go to every out_peers[i]
+  // at head out_head_offset + local head (and not to `out`).
+  int32_t n_peers;
+  int32_t out_head_offset;
+  void* out_peers[MF_MAX_OUT_PEERS];
 };
+
+// Output targets of a call (the peers' buffers, or `out`) and the address of
+// element `off` of target t.
+MF_DEVINL int out_targets(const AttnParams& p) { return p.n_peers > 0 ? p.n_peers : 1; }
+template <typename T>
+MF_DEVINL T* out_at(const AttnParams& p, int t, int64_t off) {
+  return p.n_peers > 0
+             ? static_cast<T*>(p.out_peers[t]) + off + (int64_t)p.out_head_offset * p.o_sh
+             : static_cast<T*>(p.out) + off;
+}
 
 // Query extent of sequence s.
 MF_DEVINL void seq_rows(const AttnParams& p, int s, int& q_start, int& q_len) {

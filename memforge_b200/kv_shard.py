@@ -11,10 +11,15 @@ all-gathered over NVLink with NCCL (``torch.distributed`` backend "nccl").
 MemForge itself is single-device (``memforge_ml/runtime/continuous_engine.py:164``
 takes one device); this module is the multi-GPU layer the B200 build adds.
 
-The one collective is ``all_gather_into_tensor`` of the per-rank output
-``[B, Hq/N, D]`` into ``[N*B, Hq/N, D]``, then one permute back to
-``[B, Hq, D]`` (``gather_heads``).  Every rank runs the same collectives in the
-same order.
+The outputs are assembled one of two ways:
+
+* ``gather_heads``: ``all_gather_into_tensor`` of the per-rank output
+  ``[B, Hq/N, D]`` into ``[N*B, Hq/N, D]``, then one permute back to
+  ``[B, Hq, D]``.  Every rank runs the same collectives in the same order.
+* ``PeerOutput`` (decode batches): every rank's full ``[B, Hq, D]`` output is
+  mapped into every other rank's process (CUDA IPC), the attention kernel stores
+  its heads' rows straight into all of them over NVLink, and a flag barrier
+  (``mf_peer_barrier``) completes the step.  No collective launch and no permute.
 """
 
 from __future__ import annotations
@@ -96,6 +101,97 @@ def gather_heads(local_out: torch.Tensor, group=None,
     return out
 
 
+class PeerOutput:
+    """
+    The full ``[rows, Hq, D]`` decode output of a head-sharded step, held by
+    every rank and written by all of them.
+
+    Each rank allocates one arena holding ``buffers`` output tensors and a flag
+    array of ``world`` int32, exports it through CUDA IPC (``mf_ipc_export``)
+    and maps every peer's arena into its own device's address space
+    (``mf_ipc_open``, with peer access enabled).  ``pointers(b)`` are the
+    addresses of buffer ``b`` on all GPUs as this process sees them, for
+    ``mf_attention_args.out_peers``; ``barrier()`` runs ``mf_peer_barrier`` with
+    the next epoch.  Buffers alternate per step: the barrier of step i
+    guarantees that every rank has finished step i-1, so the stores of step i+1
+    never hit a buffer a peer may still read.  Construction and ``close`` are
+    collective (all ranks, same arguments).
+    """
+
+    def __init__(self, rows: int, num_q_heads: int, head_dim: int, dtype: torch.dtype,
+                 device: torch.device, group=None, buffers: int = 2):
+        import ctypes
+        import torch.distributed as dist
+        from . import _lib as L
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        if self.world > L.MF_MAX_OUT_PEERS:
+            raise ValueError(f"peer output serves at most {L.MF_MAX_OUT_PEERS} GPUs")
+        self.device = device
+        elt = torch.empty((), dtype=dtype).element_size()
+        out_bytes = (rows * num_q_heads * head_dim * elt + 255) // 256 * 256
+        flag_off = out_bytes * buffers
+        total = flag_off + (self.world * 4 + 255) // 256 * 256
+        self.arena = torch.zeros(total, dtype=torch.uint8, device=device)
+        self.outs = [self.arena[b * out_bytes: b * out_bytes + rows * num_q_heads * head_dim * elt]
+                     .view(dtype).view(rows, num_q_heads, head_dim) for b in range(buffers)]
+        self.flags = self.arena[flag_off: flag_off + self.world * 4].view(torch.int32)
+        torch.cuda.synchronize(device)
+        lib = L.lib()
+        handle = ctypes.create_string_buffer(L.MF_IPC_HANDLE_BYTES)
+        offset = ctypes.c_uint64(0)
+        with torch.cuda.device(device):
+            L.check(lib.mf_ipc_export(ctypes.c_void_p(self.arena.data_ptr()), handle,
+                                      ctypes.byref(offset)), "mf_ipc_export")
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, (handle.raw, offset.value), group=group)
+        self._opened = []  # (address, offset) of every peer arena mapped here
+        bases = []
+        with torch.cuda.device(device):
+            for p, (h, off) in enumerate(everyone):
+                if p == self.rank:
+                    bases.append(self.arena.data_ptr())
+                    continue
+                ptr = ctypes.c_void_p(0)
+                L.check(lib.mf_ipc_open(ctypes.create_string_buffer(h, L.MF_IPC_HANDLE_BYTES),
+                                        off, ctypes.byref(ptr)), "mf_ipc_open")
+                self._opened.append((ptr.value, off))
+                bases.append(ptr.value)
+        self._ptrs = [[base + b * out_bytes for base in bases] for b in range(buffers)]
+        self.flag_ptrs = [base + flag_off for base in bases]
+        self.epoch = 0
+        dist.barrier(group=group)  # every rank has mapped every peer before first use
+
+    @property
+    def current(self) -> int:
+        """Buffer index the next step writes."""
+        return (self.epoch + 1) % len(self.outs)
+
+    def pointers(self, b: int):
+        return self._ptrs[b]
+
+    def barrier(self) -> torch.Tensor:
+        """Complete the step that wrote ``self.outs[self.current]``; return it."""
+        from . import _kernels as K
+        b = self.current
+        self.epoch += 1
+        K.peer_barrier(self.flag_ptrs, self.rank, self.epoch, self.device)
+        return self.outs[b]
+
+    def close(self) -> None:
+        """Unmap the peer arenas (collective: no rank may still write into them)."""
+        import ctypes
+        import torch.distributed as dist
+        from . import _lib as L
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for ptr, off in self._opened:
+                L.check(L.lib().mf_ipc_close(ctypes.c_void_p(ptr), off), "mf_ipc_close")
+        self._opened.clear()
+
+
 class ShardedPagedDecode:
     """
     One layer's pool shard plus the sharded KV-write + decode step.
@@ -148,3 +244,19 @@ class ShardedPagedDecode:
         if self.shard.world == 1:
             return local if out is None else out.copy_(local)
         return gather_heads(local, self.group, out=out, staging=self._staging)
+
+    def step_peer(self, peer: PeerOutput, q, new_k, new_v, slots, block_tables, kv_lens,
+                  scale=None) -> torch.Tensor:
+        """
+        The same step with the outputs assembled over peer memory: returns the full
+        ``[B, Hq, D]`` (one of ``peer``'s buffers, valid until the step after next).
+        """
+        from . import _kernels as K
+        self.write(new_k, new_v, slots)
+        b = peer.current
+        scale = scale if scale is not None else 1.0 / math.sqrt(self.head_dim)
+        K.paged_attention(self.shard.local_q(q), peer.outs[b], self.key_pool, self.value_pool,
+                          block_tables, kv_lens, q_per_seq=1, scale=scale, causal=True,
+                          out_peers=peer.pointers(b),
+                          out_head_offset=self.shard.q_range[0])
+        return peer.barrier()

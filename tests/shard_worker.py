@@ -18,7 +18,7 @@ import torch.distributed as dist
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from memforge_b200 import _kernels as K  # noqa: E402
-from memforge_b200.kv_shard import HeadShard, ShardedPagedDecode  # noqa: E402
+from memforge_b200.kv_shard import HeadShard, PeerOutput, ShardedPagedDecode  # noqa: E402
 from tests import cases  # noqa: E402
 from tests.gpu_util import torch_reference  # noqa: E402
 
@@ -53,7 +53,19 @@ def main():
     out = step.step(q, new_k, new_v, slots, tables, ctx)
     torch.cuda.synchronize()
     K.check_device_errors(dev)
-    res = {}
+    # The same step with the output assembled over peer memory (stores into every
+    # GPU's buffer + flag barrier), three steps so both buffers are reused: bit-identical.
+    peer = PeerOutput(B, Hq, D, torch.bfloat16, dev)
+    peer_equal = True
+    for _ in range(3):
+        full = step.step_peer(peer, q, new_k, new_v, slots, tables, ctx)
+        torch.cuda.synchronize()
+        K.check_device_errors(dev)
+        peer_equal = peer_equal and bool(torch.equal(full, out))
+    ok = torch.tensor([1 if peer_equal else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    peer.close()
+    res = {"peer_equal_nccl_all_ranks": bool(ok.item() == 1)}
     if rank == 0:
         # unsharded: same kernels on the full pool
         K.reshape_and_cache(new_k, new_v, kfull, vfull, slots)

@@ -1,4 +1,5 @@
-"""KV-head sharded decode on 2+ GPUs (NCCL all-gather) against the unsharded result."""
+"""KV-head sharded decode on 2+ GPUs (NCCL all-gather, and peer-memory output
+assembly) against the unsharded result."""
 
 import json
 import os
@@ -30,6 +31,7 @@ def test_sharded_decode_matches_unsharded(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     res = _run(world)
+    assert res["peer_equal_nccl_all_ranks"], res
     assert res["pool_bit_exact"]
     assert res["within_tol"], res
     assert res["max_vs_single"] < 2e-2, res
