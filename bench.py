@@ -268,29 +268,29 @@ def run_ours(args):
         collective()
     torch.cuda.synchronize(dev)
     K.check_device_errors(dev)
-    # Each kernel is captured once in a CUDA graph and replayed every step (the
-    # way MemForge's graphed decode runs), so host launch cost stays off the
-    # device timeline; events between the replays time each kernel.  With peer
-    # output there is one attention graph per output buffer.
-    g_write, n_write = capture_graph(write, dev)
-    if peer is None:
-        g_attns = [capture_graph(attend, dev)]
-    else:
-        g_attns = [capture_graph(lambda b=b: attend(b), dev) for b in range(len(peer.outs))]
-    n_attn = g_attns[0][1]
+    # The step (KV write, then attention: a programmatic dependent launch lets the
+    # attention start while the write finishes) is captured once in a CUDA graph
+    # and replayed every step, the way MemForge's graphed decode runs, so host
+    # launch cost stays off the device timeline.  With peer output there is one
+    # graph per output buffer.  Separate graphs of each kernel alone are timed
+    # with CUDA events for the roofline.
+    nbuf = 1 if peer is None else len(peer.outs)
+    g_steps = [capture_graph(lambda b=b: (write(), attend(None if peer is None else b)), dev)
+               for b in range(nbuf)]
+    n_step = g_steps[0][1]
+    g_write, _ = capture_graph(write, dev)
+    g_attns = [capture_graph(lambda b=b: attend(None if peer is None else b), dev)
+               for b in range(nbuf)]
 
-    def g_attn_replay():
-        g_attns[0 if peer is None else peer.current][0].replay()
+    def cur():
+        return 0 if peer is None else peer.current
 
     for _ in range(max(3, args.warmup)):
-        g_write.replay()
-        g_attn_replay()
+        g_steps[cur()][0].replay()
         collective()
     torch.cuda.synchronize(dev)
     K.check_device_errors(dev)
 
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
@@ -299,22 +299,31 @@ def run_ours(args):
         end_all = torch.cuda.Event(enable_timing=True)
         start_all.record(stream)
         for i in range(args.steps):
-            a, b, c = ev[i]
-            a.record(stream)
-            g_write.replay()
-            b.record(stream)
-            g_attn_replay()
-            c.record(stream)
+            g_steps[cur()][0].replay()
             collective()
         end_all.record(stream)
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     total_ms = start_all.elapsed_time(end_all)
-    decode_ms = [b.elapsed_time(c) for a, b, c in ev]
-    write_ms = [a.elapsed_time(b) for a, b, c in ev]
-    kernel_launches = (n_write + n_attn + (1 if peer is not None else 0)) * args.steps
+    kernel_launches = (n_step + (1 if peer is not None else 0)) * args.steps
     K.check_device_errors(dev)
+
+    # Each kernel alone, CUDA events around every launch, same steps count.
+    def per_launch(graphs):
+        ms = []
+        for i in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            graphs[i % len(graphs)][0].replay()
+            b.record(stream)
+            ms.append((a, b))
+        torch.cuda.synchronize(dev)
+        return [a.elapsed_time(b) for a, b in ms]
+    write_ms = per_launch([(g_write, 0)])
+    decode_ms = per_launch(g_attns)
+    if world > 1:
+        dist.barrier()
 
     t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
     if world > 1:
@@ -363,7 +372,7 @@ def run_ours(args):
                                    "sample": sample}
         print(json.dumps(res), flush=True)
     if world > 1:
-        del g_attns
+        del g_attns, g_steps
         peer.close()
         dist.barrier()
         dist.destroy_process_group()
@@ -420,12 +429,25 @@ def run_e2e(args, w, dev, kp, vp, hkv, hq, world, peer=None, rank=0):
     h_out = torch.empty((B, hq * world, D), dtype=torch.bfloat16).pin_memory()
     scale = 1.0 / math.sqrt(D)
     stream = torch.cuda.current_stream(dev)
-    d_in = [torch.empty_like(t, device=dev) for t in (h_q, h_k, h_v, h_slots, h_tab, h_ctx)]
+    # The step's host inputs sit in one pinned staging buffer, so each step
+    # makes one host-to-device copy (and one device-to-host read of the output).
+    hosts = (h_q, h_k, h_v, h_slots, h_tab, h_ctx)
+    offs, total = [], 0
+    for t in hosts:
+        offs.append(total)
+        total += (t.numel() * t.element_size() + 255) // 256 * 256
+    h_all = torch.empty(total, dtype=torch.uint8).pin_memory()
+    d_all = torch.empty(total, dtype=torch.uint8, device=dev)
+
+    def carve(buf, t, off):
+        return buf[off:off + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
+    for t, off in zip(hosts, offs):
+        carve(h_all, t, off).copy_(t)
+    d_in = [carve(d_all, t, off) for t, off in zip(hosts, offs)]
     res = {}
 
     def device_part(buf=None):
-        for d, h in zip(d_in, (h_q, h_k, h_v, h_slots, h_tab, h_ctx)):
-            d.copy_(h, non_blocking=True)
+        d_all.copy_(h_all, non_blocking=True)
         q, k, v, sl, tab, cx = d_in
         K.reshape_and_cache(k, v, kp, vp, sl)
         if world == 1:
@@ -467,7 +489,7 @@ def run_e2e(args, w, dev, kp, vp, hkv, hq, world, peer=None, rank=0):
         ms = timed(lambda: (gs[peer.current].replay(), tail()))
         g = gs
     attn_b, write_b = algorithmic_bytes(w, hkv, hq)
-    bi = sum(t.numel() * t.element_size() for t in (h_q, h_k, h_v, h_slots, h_tab, h_ctx))
+    bi = h_all.numel()
     bo = h_out.numel() * h_out.element_size()
     del g
     return {"value": round((attn_b + write_b) * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",

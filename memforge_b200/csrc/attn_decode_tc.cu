@@ -845,6 +845,9 @@ __global__ void __launch_bounds__(THREADS, 1) decode_kernel(
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // Everything above overlaps the previous kernel (programmatic launch);
+  // nothing in global memory is read before this point.
+  grid_dependency_wait();
   for (int i = tid; i < B; i += blockDim.x) {
     const SeqGeo g = seq_geo(P, i);
     const bool other = P.skip_long && g.q_len * P.G > P.rows_cap;
@@ -1091,7 +1094,19 @@ static int launch_tc_t(const AttnParams& p, const TcPlan& pl, void* ws, cudaStre
       return fail(MF_ECUDA, std::string("paged attention: ") + cudaGetErrorString(e));
     configured_dev[pl.SW] = dev;
   }
-  kern<<<pl.ctas, tc::THREADS, pl.smem, stream>>>(mk, mv, mwk, mwv, P);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)pl.ctas);
+  cfg.blockDim = dim3(tc::THREADS);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, kern, mk, mv, mwk, mwv, P);
+  if (le != cudaSuccess)
+    return fail(MF_ECUDA, std::string("paged attention (tcgen05 decode): ") + cudaGetErrorString(le));
   return check_launch("paged attention (tensor-core decode)");
 }
 

@@ -219,6 +219,9 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     fence_barrier_init();
   }
   for (int i = tid; i < NBK; i += THREADS) counts[i] = 0;
+  // Everything above overlaps the previous kernel (programmatic launch);
+  // nothing in global memory is read before this point.
+  grid_dependency_wait();
   if (warp == 0) {
     tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
@@ -821,7 +824,19 @@ int launch_attn_prefill_tc(const AttnParams& p, mf_dtype dtype, int rows_cap,
     if (e != cudaSuccess) return fail(MF_ECUDA, std::string("prefill: ") + cudaGetErrorString(e));
     configured_dev[which] = dev;
   }
-  kern<<<(unsigned)grid, pf::THREADS, smem, stream>>>(mq, mk, mv, mwk, mwv, P);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(pf::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t le = cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mwk, mwv, P);
+  if (le != cudaSuccess)
+    return fail(MF_ECUDA, std::string("prefill: ") + cudaGetErrorString(le));
   return check_launch("paged attention (tcgen05 prefill)");
 }
 

@@ -21,6 +21,9 @@ __global__ void reshape_and_cache_kernel(const S* __restrict__ key, const S* __r
                                          int32_t block_size, const void* __restrict__ slots,
                                          int slots64, int num_tokens, int num_heads,
                                          int head_dim, int vec, int32_t* err) {
+  // The attention kernel that usually follows may be scheduled now: it waits
+  // for this kernel's completion before it reads anything.
+  grid_launch_dependents();
   // One work item = (token, head, vector of `vec` elements along head_dim).
   const int vecs_per_row = head_dim / vec;
   const int64_t total = (int64_t)num_tokens * num_heads * vecs_per_row;

@@ -108,6 +108,14 @@ MF_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_
   }
 }
 
+// Programmatic dependent launch: a kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may start while the
+// previous kernel on its stream runs; grid_dependency_wait() blocks until that
+// kernel has completed and its memory is visible (a no-op otherwise), and
+// grid_launch_dependents() lets the next such kernel start early.
+MF_DEVINL void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MF_DEVINL void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 MF_DEVINL void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
