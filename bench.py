@@ -353,7 +353,7 @@ def run_ours(args):
                        "batch": B, "kv_heads_per_gpu": hkv, "sum_ctx": int(w["ctx"].sum()),
                        "pool_blocks": NB, "parallelism": f"kv-head shard x{world}" if world > 1 else "1 GPU",
                        "l2": "inputs exceed L2 (KV read per step > 126 MB); no flush",
-                       "launch": "each kernel captured once in a CUDA graph, replayed every step"},
+                       "launch": "the step (KV write, then decode as a programmatic dependent launch) captured once as one CUDA graph, replayed every step"},
             "attn_tokens_per_s": round(B * W * world / (ms_step * 1e-3), 1) if world == 1 else round(B * W / (ms_step * 1e-3), 1),
             "roofline": {"bound": "hbm", "kernel": "paged decode (tc::decode_kernel)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
