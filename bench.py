@@ -689,11 +689,15 @@ def run_cfg4(args):
     def verify():
         verify_attention(q, wk, wv, kp, vp, tables, ctx, out=out, kv_lens=kvl)
 
+    def commit():
+        commit_accepted(kp, vp, wk, wv, tables, ctx, acc)
+
     def step():
         verify()
-        commit_accepted(kp, vp, wk, wv, tables, ctx, acc)
+        commit()
     ms = _time(step, args.steps, args.warmup, dev)
     ms_v = _time(verify, args.steps, args.warmup, dev)
+    ms_c = _time(commit, args.steps, args.warmup, dev)
     K.check_device_errors(dev)
     ctxn = meta["ctx"].astype(np.int64)
     vbytes = int(ctxn.sum()) * 2 * Hkv * D * 2 + B * W * (Hq * D * 2 * 2 + Hkv * D * 2 * 2) + \
@@ -701,6 +705,7 @@ def run_cfg4(args):
     peak, kind = measured_peaks()
     res = {"metric": "speculative verify attention HBM GB/s (BASELINE config 4)",
            "ms_per_step": round(ms, 4), "verify_ms": round(ms_v, 4),
+           "commit_ms": round(ms_c, 4), "committed_rows": int((meta["accepted"] + 1).sum()),
            "verify_GBs": round(vbytes / (ms_v * 1e-3) / 1e9, 1),
            "verify_frac_of_measured_peak": round(vbytes / (ms_v * 1e-3) / 1e9 / peak, 4),
            "attn_tokens_per_s": round(B * W / (ms * 1e-3), 1), "dtype": "bf16"}

@@ -35,7 +35,7 @@ _workspaces: Dict[int, torch.Tensor] = {}
 _err_words: Dict[int, torch.Tensor] = {}
 _checks = os.environ.get("MEMFORGE_CHECK", "0") not in ("", "0")
 launch_counter = {"reshape_and_cache": 0, "paged_attention": 0, "copy_blocks": 0,
-                  "peer_barrier": 0}
+                  "peer_barrier": 0, "commit_window": 0}
 
 
 def set_checks(enabled: bool) -> None:
@@ -167,6 +167,57 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_pool: torch.Te
     L.check(rc, "mf_reshape_and_cache")
     launch_counter["reshape_and_cache"] += 1
     _after("reshape_and_cache", dev)
+
+
+def commit_window(win_k: torch.Tensor, win_v: torch.Tensor, key_pool: torch.Tensor,
+                  value_pool: torch.Tensor, block_tables: torch.Tensor, ctx_lens: torch.Tensor,
+                  num_confirmed: torch.Tensor) -> None:
+    """
+    Write rows ``0 .. num_confirmed[b]-1`` of each sequence's window into the
+    pool at positions ``ctx_lens[b] + j`` (one launch; the slot arithmetic runs
+    on the device).  ``win_k``/``win_v`` are ``(B*W, H, D)`` sequence-major,
+    ``key_pool`` one layer ``(blocks, block_size, H, D)``, ``block_tables``
+    int32 ``[B, width]``, ``ctx_lens`` and ``num_confirmed`` int32 ``[B]``.
+    Rows past ``num_confirmed`` are not written.
+    """
+    require_cuda("commit_window", win_k, win_v, key_pool, value_pool, block_tables, ctx_lens,
+                 num_confirmed)
+    if win_k.dim() != 3 or win_v.shape != win_k.shape:
+        raise ValueError(f"window keys/values must be (B*W, H, D) of one shape, got "
+                         f"{tuple(win_k.shape)} and {tuple(win_v.shape)}")
+    B = ctx_lens.numel()
+    if B == 0:
+        return
+    if num_confirmed.numel() != B:
+        raise ValueError(f"{B} sequences but {num_confirmed.numel()} confirmed counts")
+    W = win_k.shape[0] // B
+    if W * B != win_k.shape[0] or W == 0:
+        raise ValueError("window rows are not a whole number of windows")
+    if win_k.stride(-1) != 1:
+        win_k = win_k.contiguous()
+    if win_v.stride(-1) != 1:
+        win_v = win_v.contiguous()
+    if key_pool.stride(-1) != 1 or value_pool.stride() != key_pool.stride():
+        raise ValueError("pool layers must share strides and have a contiguous last dim")
+    nb, bs, hp, dp = key_pool.shape
+    _, H, D = win_k.shape
+    if (hp, dp) != (H, D):
+        raise ValueError(f"pool holds {hp} heads x {dp} dims, window rows are {H} x {D}")
+    if block_tables.dim() != 2 or block_tables.shape[0] != B:
+        raise ValueError("block_tables must be [B, width]")
+    tables = block_tables.to(torch.int32).contiguous()
+    ctx = ctx_lens.to(torch.int32).contiguous()
+    conf = num_confirmed.to(torch.int32).contiguous()
+    dev = win_k.device
+    rc = L.lib().mf_commit_window(
+        win_k.data_ptr(), win_v.data_ptr(), dtype_code(win_k.dtype), win_k.stride(0),
+        win_k.stride(1), win_v.stride(0), win_v.stride(1), key_pool.data_ptr(),
+        value_pool.data_ptr(), dtype_code(key_pool.dtype), key_pool.stride(0),
+        key_pool.stride(1), key_pool.stride(2), nb, bs, tables.data_ptr(), tables.stride(0),
+        ctx.data_ptr(), conf.data_ptr(), B, W, H, D, err_word(dev).data_ptr(), _stream_ptr(dev))
+    L.check(rc, "mf_commit_window")
+    launch_counter["commit_window"] += 1
+    _after("commit_window", dev)
 
 
 def copy_blocks(key_pool: torch.Tensor, value_pool: torch.Tensor, pairs: torch.Tensor) -> None:

@@ -1,5 +1,6 @@
-// KV writes into the paged pool: reshape_and_cache (slot-mapping scatter) and
-// the all-layer copy-on-write block copy.
+// KV writes into the paged pool: reshape_and_cache (slot-mapping scatter), the
+// speculative commit of a window's confirmed rows, and the all-layer
+// copy-on-write block copy.
 //
 // Both are byte-moving kernels bounded by HBM: every thread moves one 16-byte
 // vector (8 bf16 / 4 fp32 elements) when the row is 16-byte aligned, so each
@@ -65,6 +66,61 @@ MF_DEVINL void copy_row_vec(const S* __restrict__ src, P* __restrict__ dst, int 
   }
 }
 
+// Speculative commit: row j of sequence b's window goes to pool position
+// ctx[b] + j, through b's block table, for j < num_confirmed[b]; the other rows
+// (rejected drafts) are not written, so their slots keep what they held.  The
+// slot arithmetic of PagedKVPool.slot_indices (memforge_ml/runtime/
+// kv_pool.py:92-130) runs on the device; a position past the table row or a
+// block id outside the pool sets an error bit and skips the row, as the
+// reference's IndexError would stop the write.
+template <typename S, typename P>
+__global__ void commit_window_kernel(const S* __restrict__ wk, const S* __restrict__ wv,
+                                     int64_t k_stride_row, int64_t k_stride_head,
+                                     int64_t v_stride_row, int64_t v_stride_head,
+                                     P* __restrict__ key_pool, P* __restrict__ value_pool,
+                                     int64_t sb, int64_t ss, int64_t sh, int32_t num_blocks,
+                                     int32_t block_size, const int32_t* __restrict__ tables,
+                                     int32_t table_stride, const int32_t* __restrict__ ctx_lens,
+                                     const int32_t* __restrict__ num_confirmed, int num_seqs,
+                                     int window, int num_heads, int head_dim, int vec,
+                                     int32_t* err) {
+  const int vecs_per_row = head_dim / vec;
+  const int64_t total = (int64_t)num_seqs * window * num_heads * vecs_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vecs_per_row);
+    const int64_t rh = i / vecs_per_row;
+    const int h = (int)(rh % num_heads);
+    const int64_t r = rh / num_heads;  // window row, sequence-major
+    const int b = (int)(r / window), j = (int)(r % window);
+    const bool lead = v == 0 && h == 0;
+    const int n = __ldg(num_confirmed + b);
+    const int c = __ldg(ctx_lens + b);
+    if (n < 0 || n > window || c < 0) {
+      if (lead && j == 0) set_err(err, MF_ERR_LENGTH);
+      continue;
+    }
+    if (j >= n) continue;
+    const int64_t pos = (int64_t)c + j;
+    const int64_t page = pos / block_size;
+    if (page >= table_stride) {
+      if (lead) set_err(err, MF_ERR_TABLE);
+      continue;
+    }
+    const int blk = __ldg(tables + (int64_t)b * table_stride + page);
+    if (blk < 0 || blk >= num_blocks) {
+      if (lead) set_err(err, MF_ERR_BLOCK_ID);
+      continue;
+    }
+    const int64_t dst_off =
+        (int64_t)blk * sb + (pos % block_size) * ss + h * sh + (int64_t)v * vec;
+    copy_row_vec<S, P>(wk + r * k_stride_row + h * k_stride_head + (int64_t)v * vec,
+                       key_pool + dst_off, vec);
+    copy_row_vec<S, P>(wv + r * v_stride_row + h * v_stride_head + (int64_t)v * vec,
+                       value_pool + dst_off, vec);
+  }
+}
+
 __global__ void copy_blocks_kernel(uint8_t* __restrict__ kp, uint8_t* __restrict__ vp,
                                    int num_layers, int num_blocks, int64_t block_bytes,
                                    const int32_t* __restrict__ pairs, int num_pairs,
@@ -123,6 +179,32 @@ int launch_rac(const void* key, const void* value, int64_t kst, int64_t ksh, int
       static_cast<P*>(kp), static_cast<P*>(vp), sb, ss, sh, num_slots, bs, slots, slots64, T, H,
       D, vec, err);
   return check_launch("reshape_and_cache");
+}
+
+template <typename S, typename P>
+int launch_commit(const void* wk, const void* wv, int64_t kst, int64_t ksh, int64_t vst,
+                  int64_t vsh, void* kp, void* vp, int64_t sb, int64_t ss, int64_t sh, int32_t nb,
+                  int32_t bs, const int32_t* tables, int32_t table_stride, const int32_t* ctx,
+                  const int32_t* conf, int B, int W, int H, int D, int32_t* err,
+                  cudaStream_t stream) {
+  int vec = 1;
+  const int v16 = 16 / (int)sizeof(P);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (std::is_same<S, P>::value && D % v16 == 0 && al(wk) && al(wv) && al(kp) && al(vp) &&
+      (kst * sizeof(S)) % 16 == 0 && (ksh * sizeof(S)) % 16 == 0 &&
+      (vst * sizeof(S)) % 16 == 0 && (vsh * sizeof(S)) % 16 == 0 &&
+      (sb * sizeof(P)) % 16 == 0 && (ss * sizeof(P)) % 16 == 0 && (sh * sizeof(P)) % 16 == 0) {
+    vec = v16;
+  }
+  const int64_t items = (int64_t)B * W * H * (D / vec);
+  const int threads = 256;
+  int64_t blocks = (items + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  commit_window_kernel<S, P><<<(unsigned)blocks, threads, 0, stream>>>(
+      static_cast<const S*>(wk), static_cast<const S*>(wv), kst, ksh, vst, vsh,
+      static_cast<P*>(kp), static_cast<P*>(vp), sb, ss, sh, nb, bs, tables, table_stride, ctx,
+      conf, B, W, H, D, vec, err);
+  return check_launch("commit_window");
 }
 
 }  // namespace
@@ -185,4 +267,40 @@ extern "C" int mf_copy_blocks(void* key_pool, void* value_pool, int32_t num_laye
       static_cast<uint8_t*>(key_pool), static_cast<uint8_t*>(value_pool), num_layers, num_blocks,
       block_bytes, src_dst_pairs, num_pairs, err_flag);
   return check_launch("copy_blocks");
+}
+
+extern "C" int mf_commit_window(const void* win_k, const void* win_v, mf_dtype src_dtype,
+                                int64_t k_stride_row, int64_t k_stride_head, int64_t v_stride_row,
+                                int64_t v_stride_head, void* key_pool, void* value_pool,
+                                mf_dtype pool_dtype, int64_t pool_stride_block,
+                                int64_t pool_stride_slot, int64_t pool_stride_head,
+                                int32_t num_blocks, int32_t block_size,
+                                const int32_t* block_tables, int32_t table_stride,
+                                const int32_t* ctx_lens, const int32_t* num_confirmed,
+                                int32_t num_seqs, int32_t window, int32_t num_kv_heads,
+                                int32_t head_dim, int32_t* err_flag, mf_stream_t stream) {
+  if (num_seqs < 0 || window <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks <= 0 || table_stride < 0)
+    return fail(MF_EINVAL, "commit_window: non-positive size");
+  if (num_seqs == 0) return MF_OK;
+  if (!win_k || !win_v || !key_pool || !value_pool || !block_tables || !ctx_lens ||
+      !num_confirmed)
+    return fail(MF_EINVAL, "commit_window: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+#define MF_COMMIT(S, P)                                                                        \
+  return launch_commit<S, P>(win_k, win_v, k_stride_row, k_stride_head, v_stride_row,           \
+                             v_stride_head, key_pool, value_pool, pool_stride_block,            \
+                             pool_stride_slot, pool_stride_head, num_blocks, block_size,        \
+                             block_tables, table_stride, ctx_lens, num_confirmed, num_seqs,     \
+                             window, num_kv_heads, head_dim, err_flag, s)
+  if (src_dtype == pool_dtype) {
+    if (pool_dtype == MF_F32) MF_COMMIT(float, float);
+    if (pool_dtype == MF_F16) MF_COMMIT(__half, __half);
+    if (pool_dtype == MF_BF16) MF_COMMIT(__nv_bfloat16, __nv_bfloat16);
+  } else if (src_dtype == MF_F32) {
+    if (pool_dtype == MF_F16) MF_COMMIT(float, __half);
+    if (pool_dtype == MF_BF16) MF_COMMIT(float, __nv_bfloat16);
+  }
+#undef MF_COMMIT
+  return fail(MF_EUNSUPPORTED, "commit_window: unsupported (src, pool) dtype pair");
 }

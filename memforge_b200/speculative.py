@@ -67,11 +67,14 @@ def commit_slots(block_tables: torch.Tensor, ctx_lens: torch.Tensor, num_confirm
 def commit_accepted(key_layer: torch.Tensor, value_layer: torch.Tensor, win_k: torch.Tensor,
                     win_v: torch.Tensor, block_tables: torch.Tensor, ctx_lens: torch.Tensor,
                     num_confirmed: torch.Tensor, block_size: int = 16) -> None:
-    """Write the first ``num_confirmed[b]`` window rows of each sequence into the pool."""
-    B = ctx_lens.numel()
-    W = win_k.shape[0] // B
-    slots = commit_slots(block_tables, ctx_lens, num_confirmed, W, block_size)
-    K.reshape_and_cache(win_k, win_v, key_layer, value_layer, slots)
+    """
+    Write the first ``num_confirmed[b]`` window rows of each sequence into the
+    pool: one ``mf_commit_window`` launch (positions ``ctx .. ctx+n-1`` through
+    the block table on the device; the rejected rows' slots are left alone).
+    """
+    if key_layer.shape[1] != block_size:
+        raise ValueError(f"pool block size {key_layer.shape[1]} != {block_size}")
+    K.commit_window(win_k, win_v, key_layer, value_layer, block_tables, ctx_lens, num_confirmed)
 
 
 def scatter_accepted_kv(pool, block_table: torch.Tensor, context_length: int,

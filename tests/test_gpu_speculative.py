@@ -77,3 +77,84 @@ def test_verify_then_commit_round_trip():
     got_v = vp.cpu().view(torch.int16).numpy().view(np.uint16)
     assert np.array_equal(got_k, want_k[0]), "pool after commit differs from the reference commit"
     assert np.array_equal(got_v, want_v[0])
+
+
+def _commit_case(seed, ctx, W, H=2, D=64, width=6):
+    """Pool, disjoint block tables (no slot is named twice) and fp32 windows."""
+    g = np.random.default_rng(seed)
+    B = len(ctx)
+    NB = B * width + 4
+    kp0 = g.standard_normal((NB, 16, H, D)).astype(np.float32)
+    vp0 = g.standard_normal((NB, 16, H, D)).astype(np.float32)
+    tables = g.permutation(NB)[:B * width].reshape(B, width).astype(np.int32)
+    wk = g.standard_normal((B * W, H, D)).astype(np.float32)
+    wv = g.standard_normal((B * W, H, D)).astype(np.float32)
+    return kp0, vp0, tables, wk, wv
+
+
+def _oracle_commit(kp0, vp0, tables, ctx, wk, wv, conf, W, src, pool):
+    want_k = O.from_f32(kp0, pool)[None].copy()
+    want_v = O.from_f32(vp0, pool)[None].copy()
+    for s, n in enumerate(conf):
+        k = O.from_f32(np.transpose(wk[s * W:(s + 1) * W], (1, 0, 2)), src)[None]
+        v = O.from_f32(np.transpose(wv[s * W:(s + 1) * W], (1, 0, 2)), src)[None]
+        if n <= 0:
+            continue
+        flat = O.flat_indices(tables[s], ctx[s], ctx[s] + n, 16)
+        O.scatter_kv(want_k, want_v, 0, flat, k[:, :, :n], v[:, :, :n], pool, src)
+    return want_k[0], want_v[0]
+
+
+def _bits(t):
+    if t.dtype == torch.float32:
+        return t.cpu().view(torch.int32).numpy()
+    return t.cpu().view(torch.int16).numpy()
+
+
+def _want_bits(a, dt):
+    return a.view(np.int32) if dt == "f32" else a.view(np.int16)
+
+
+@pytest.mark.parametrize("src,pool", [("bf16", "bf16"), ("f16", "f16"), ("f32", "f32"),
+                                      ("f32", "bf16")])
+def test_commit_window_bit_exact_with_page_crossings(src, pool):
+    """One launch commits each window's confirmed prefix (0..W rows, across page
+    boundaries); the rejected rows' slots keep their old bytes."""
+    from memforge_b200 import _kernels as K
+    W = 5
+    ctx = [0, 13, 15, 16, 30, 47, 60]
+    conf = [1, 5, 3, 0, 4, 5, 2]
+    kp0, vp0, tables, wk, wv = _commit_case(40, ctx, W)
+    # torch's fp32 -> bf16/f16 casts round to nearest even, like the oracle's
+    kp, vp = to_dev(kp0, pool), to_dev(vp0, pool)
+    dk, dv = to_dev(wk, src), to_dev(wv, src)
+    K.commit_window(dk, dv, kp, vp, torch.from_numpy(tables).cuda(),
+                    torch.tensor(ctx, dtype=torch.int32, device="cuda"),
+                    torch.tensor(conf, dtype=torch.int32, device="cuda"))
+    K.check_device_errors(kp.device)
+    want_k, want_v = _oracle_commit(kp0, vp0, tables, ctx, wk, wv, conf, W, src, pool)
+    assert np.array_equal(_bits(kp), _want_bits(want_k, pool))
+    assert np.array_equal(_bits(vp), _want_bits(want_v, pool))
+
+
+def test_commit_window_errors_skip_rows_and_set_bits():
+    from memforge_b200 import _kernels as K
+    W, width = 4, 2
+    ctx = [30, 5, 5, 5]
+    conf = [4, 5, 2, 1]   # seq 0 crosses past its 2-page table; seq 1 confirms more than W
+    kp0, vp0, tables, wk, wv = _commit_case(41, ctx, W, width=width)
+    tables[3, 0] = 999    # block id outside the pool
+    kp, vp = to_dev(kp0, "bf16"), to_dev(vp0, "bf16")
+    dk, dv = to_dev(wk, "bf16"), to_dev(wv, "bf16")
+    K.commit_window(dk, dv, kp, vp, torch.from_numpy(tables).cuda(),
+                    torch.tensor(ctx, dtype=torch.int32, device="cuda"),
+                    torch.tensor(conf, dtype=torch.int32, device="cuda"))
+    bits = int(K.err_word(kp.device).item())
+    with pytest.raises(IndexError):
+        K.check_device_errors(kp.device)
+    assert bits == 0x1 | 0x4 | 0x8, hex(bits)
+    # What the kernel still writes: seq 0's rows inside the table (positions 30, 31),
+    # all of seq 2's confirmed rows; nothing of seq 1 or seq 3.
+    want_k, _ = _oracle_commit(kp0, vp0, tables, [30, 5, 5, 5],
+                               wk, wv, [2, 0, 2, 0], W, "bf16", "bf16")
+    assert np.array_equal(_bits(kp), _want_bits(want_k, "bf16"))
