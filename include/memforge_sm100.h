@@ -248,27 +248,31 @@ MF_API int mf_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_
 
 /*
  * commit_window — write the confirmed prefix of each speculative window into
- * the pool, in one launch.
+ * the pool, for every layer, in one launch.
  *
  * Replaces scatter_accepted_kv (memforge_ml/runtime/batched_speculative.py:
- * 780-811) with its slot arithmetic (PagedKVPool.slot_indices,
- * memforge_ml/runtime/kv_pool.py:92-130): window row j of sequence b (row
- * b*window + j of win_k / win_v) lands at pool position ctx_lens[b] + j, i.e.
- * slot block_tables[b*table_stride + pos/block_size]*block_size +
- * pos%block_size, for j < num_confirmed[b] (the last confirmed token plus
- * the accepted drafts).  Rows j >= num_confirmed[b] are not written, so the
- * rejected slots keep their contents, as in the reference.  num_confirmed
- * outside [0, window] sets MF_ERR_LENGTH, a position past the table row
- * MF_ERR_TABLE, a block id outside the pool MF_ERR_BLOCK_ID (the row is
- * skipped).  Dtype pairs and rounding as mf_reshape_and_cache.  All integer
- * inputs live on the device, so the call is CUDA-graph safe.
+ * 780-811), which the batched engine calls per sequence and writes per layer,
+ * with its slot arithmetic (PagedKVPool.slot_indices,
+ * memforge_ml/runtime/kv_pool.py:92-130): in layer l, window row j of sequence
+ * b (element (l, b*window + j, h, d) at win_k + l*k_stride_layer +
+ * (b*window + j)*k_stride_row + h*k_stride_head + d) lands at pool position
+ * ctx_lens[b] + j, i.e. slot block_tables[b*table_stride + pos/block_size]*
+ * block_size + pos%block_size of layer l (pool_stride_layer apart), for
+ * j < num_confirmed[b] (the last confirmed token plus the accepted drafts).
+ * Rows j >= num_confirmed[b] are not written, so the rejected slots keep their
+ * contents, as in the reference.  num_confirmed outside [0, window] sets
+ * MF_ERR_LENGTH, a position past the table row MF_ERR_TABLE, a block id
+ * outside the pool MF_ERR_BLOCK_ID (the row is skipped in every layer).
+ * Dtype pairs and rounding as mf_reshape_and_cache.  All integer inputs live
+ * on the device, so the call is CUDA-graph safe.
  */
 MF_API int mf_commit_window(const void* win_k, const void* win_v, mf_dtype src_dtype,
-                     int64_t k_stride_row, int64_t k_stride_head,
-                     int64_t v_stride_row, int64_t v_stride_head,
+                     int64_t k_stride_layer, int64_t k_stride_row, int64_t k_stride_head,
+                     int64_t v_stride_layer, int64_t v_stride_row, int64_t v_stride_head,
                      void* key_pool, void* value_pool, mf_dtype pool_dtype,
-                     int64_t pool_stride_block, int64_t pool_stride_slot,
-                     int64_t pool_stride_head, int32_t num_blocks, int32_t block_size,
+                     int64_t pool_stride_layer, int64_t pool_stride_block,
+                     int64_t pool_stride_slot, int64_t pool_stride_head,
+                     int32_t num_layers, int32_t num_blocks, int32_t block_size,
                      const int32_t* block_tables, int32_t table_stride,
                      const int32_t* ctx_lens, const int32_t* num_confirmed,
                      int32_t num_seqs, int32_t window, int32_t num_kv_heads,

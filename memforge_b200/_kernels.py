@@ -175,32 +175,44 @@ def commit_window(win_k: torch.Tensor, win_v: torch.Tensor, key_pool: torch.Tens
     """
     Write rows ``0 .. num_confirmed[b]-1`` of each sequence's window into the
     pool at positions ``ctx_lens[b] + j`` (one launch; the slot arithmetic runs
-    on the device).  ``win_k``/``win_v`` are ``(B*W, H, D)`` sequence-major,
-    ``key_pool`` one layer ``(blocks, block_size, H, D)``, ``block_tables``
-    int32 ``[B, width]``, ``ctx_lens`` and ``num_confirmed`` int32 ``[B]``.
-    Rows past ``num_confirmed`` are not written.
+    on the device).  One layer: ``win_k``/``win_v`` ``(B*W, H, D)``
+    sequence-major and ``key_pool`` ``(blocks, block_size, H, D)``; every layer
+    at once: ``(L, B*W, H, D)`` windows and ``(L, blocks, block_size, H, D)``
+    pools.  ``block_tables`` int32 ``[B, width]``, ``ctx_lens`` and
+    ``num_confirmed`` int32 ``[B]``.  Rows past ``num_confirmed`` are not
+    written.
     """
     require_cuda("commit_window", win_k, win_v, key_pool, value_pool, block_tables, ctx_lens,
                  num_confirmed)
-    if win_k.dim() != 3 or win_v.shape != win_k.shape:
-        raise ValueError(f"window keys/values must be (B*W, H, D) of one shape, got "
-                         f"{tuple(win_k.shape)} and {tuple(win_v.shape)}")
+    if win_v.shape != win_k.shape or win_k.dim() not in (3, 4):
+        raise ValueError(f"window keys/values must be (B*W, H, D) or (L, B*W, H, D) of one "
+                         f"shape, got {tuple(win_k.shape)} and {tuple(win_v.shape)}")
+    layered = win_k.dim() == 4
+    if key_pool.dim() != (5 if layered else 4) or value_pool.shape != key_pool.shape:
+        raise ValueError("pools must be (blocks, block_size, H, D) for (B*W, H, D) windows and "
+                         "(L, blocks, block_size, H, D) for (L, B*W, H, D) windows")
+    wk = win_k if layered else win_k.unsqueeze(0)
+    wv = win_v if layered else win_v.unsqueeze(0)
+    kp = key_pool if layered else key_pool.unsqueeze(0)
+    vp = value_pool if layered else value_pool.unsqueeze(0)
     B = ctx_lens.numel()
     if B == 0:
         return
     if num_confirmed.numel() != B:
         raise ValueError(f"{B} sequences but {num_confirmed.numel()} confirmed counts")
-    W = win_k.shape[0] // B
-    if W * B != win_k.shape[0] or W == 0:
+    L_, R, H, D = wk.shape
+    W = R // B
+    if W * B != R or W == 0:
         raise ValueError("window rows are not a whole number of windows")
-    if win_k.stride(-1) != 1:
-        win_k = win_k.contiguous()
-    if win_v.stride(-1) != 1:
-        win_v = win_v.contiguous()
-    if key_pool.stride(-1) != 1 or value_pool.stride() != key_pool.stride():
-        raise ValueError("pool layers must share strides and have a contiguous last dim")
-    nb, bs, hp, dp = key_pool.shape
-    _, H, D = win_k.shape
+    if kp.shape[0] != L_:
+        raise ValueError(f"{L_} window layers but {kp.shape[0]} pool layers")
+    if wk.stride(-1) != 1:
+        wk = wk.contiguous()
+    if wv.stride(-1) != 1:
+        wv = wv.contiguous()
+    if kp.stride(-1) != 1 or vp.stride() != kp.stride():
+        raise ValueError("pools must share strides and have a contiguous last dim")
+    _, nb, bs, hp, dp = kp.shape
     if (hp, dp) != (H, D):
         raise ValueError(f"pool holds {hp} heads x {dp} dims, window rows are {H} x {D}")
     if block_tables.dim() != 2 or block_tables.shape[0] != B:
@@ -210,11 +222,11 @@ def commit_window(win_k: torch.Tensor, win_v: torch.Tensor, key_pool: torch.Tens
     conf = num_confirmed.to(torch.int32).contiguous()
     dev = win_k.device
     rc = L.lib().mf_commit_window(
-        win_k.data_ptr(), win_v.data_ptr(), dtype_code(win_k.dtype), win_k.stride(0),
-        win_k.stride(1), win_v.stride(0), win_v.stride(1), key_pool.data_ptr(),
-        value_pool.data_ptr(), dtype_code(key_pool.dtype), key_pool.stride(0),
-        key_pool.stride(1), key_pool.stride(2), nb, bs, tables.data_ptr(), tables.stride(0),
-        ctx.data_ptr(), conf.data_ptr(), B, W, H, D, err_word(dev).data_ptr(), _stream_ptr(dev))
+        wk.data_ptr(), wv.data_ptr(), dtype_code(wk.dtype), wk.stride(0), wk.stride(1),
+        wk.stride(2), wv.stride(0), wv.stride(1), wv.stride(2), kp.data_ptr(), vp.data_ptr(),
+        dtype_code(kp.dtype), kp.stride(0), kp.stride(1), kp.stride(2), kp.stride(3), L_, nb, bs,
+        tables.data_ptr(), tables.stride(0), ctx.data_ptr(), conf.data_ptr(), B, W, H, D,
+        err_word(dev).data_ptr(), _stream_ptr(dev))
     L.check(rc, "mf_commit_window")
     launch_counter["commit_window"] += 1
     _after("commit_window", dev)

@@ -105,9 +105,9 @@ def _declare(lib):
         c_i32, c_i32, c_i32, c_i32, c_f32, ctypes.c_int, c_vp, c_vp, c_sz, c_vp, c_vp]
     lib.mf_copy_blocks.argtypes = [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp, c_vp]
     lib.mf_commit_window.argtypes = [
-        c_vp, c_vp, ctypes.c_int, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp, ctypes.c_int,
-        c_i64, c_i64, c_i64, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32,
-        c_vp, c_vp]
+        c_vp, c_vp, ctypes.c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,
+        ctypes.c_int, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_vp, c_i32, c_vp, c_vp,
+        c_i32, c_i32, c_i32, c_i32, c_vp, c_vp]
     lib.mf_peer_barrier.argtypes = [ctypes.POINTER(c_vp), c_i32, c_i32, ctypes.c_uint32, c_vp,
                                      c_vp]
     lib.mf_ipc_export.argtypes = [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]

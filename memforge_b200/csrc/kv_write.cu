@@ -66,7 +66,8 @@ MF_DEVINL void copy_row_vec(const S* __restrict__ src, P* __restrict__ dst, int 
   }
 }
 
-// Speculative commit: row j of sequence b's window goes to pool position
+// Speculative commit, all layers in one launch: row j of sequence b's window
+// goes to pool position
 // ctx[b] + j, through b's block table, for j < num_confirmed[b]; the other rows
 // (rejected drafts) are not written, so their slots keep what they held.  The
 // slot arithmetic of PagedKVPool.slot_indices (memforge_ml/runtime/
@@ -75,25 +76,30 @@ MF_DEVINL void copy_row_vec(const S* __restrict__ src, P* __restrict__ dst, int 
 // reference's IndexError would stop the write.
 template <typename S, typename P>
 __global__ void commit_window_kernel(const S* __restrict__ wk, const S* __restrict__ wv,
-                                     int64_t k_stride_row, int64_t k_stride_head,
+                                     int64_t k_stride_layer, int64_t k_stride_row,
+                                     int64_t k_stride_head, int64_t v_stride_layer,
                                      int64_t v_stride_row, int64_t v_stride_head,
                                      P* __restrict__ key_pool, P* __restrict__ value_pool,
-                                     int64_t sb, int64_t ss, int64_t sh, int32_t num_blocks,
-                                     int32_t block_size, const int32_t* __restrict__ tables,
-                                     int32_t table_stride, const int32_t* __restrict__ ctx_lens,
+                                     int64_t sl, int64_t sb, int64_t ss, int64_t sh,
+                                     int num_layers, int32_t num_blocks, int32_t block_size,
+                                     const int32_t* __restrict__ tables, int32_t table_stride,
+                                     const int32_t* __restrict__ ctx_lens,
                                      const int32_t* __restrict__ num_confirmed, int num_seqs,
                                      int window, int num_heads, int head_dim, int vec,
                                      int32_t* err) {
   const int vecs_per_row = head_dim / vec;
-  const int64_t total = (int64_t)num_seqs * window * num_heads * vecs_per_row;
+  const int64_t per_layer = (int64_t)num_seqs * window * num_heads * vecs_per_row;
+  const int64_t total = per_layer * num_layers;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int v = (int)(i % vecs_per_row);
-    const int64_t rh = i / vecs_per_row;
+    const int layer = (int)(i / per_layer);
+    const int64_t li = i - (int64_t)layer * per_layer;
+    const int v = (int)(li % vecs_per_row);
+    const int64_t rh = li / vecs_per_row;
     const int h = (int)(rh % num_heads);
     const int64_t r = rh / num_heads;  // window row, sequence-major
     const int b = (int)(r / window), j = (int)(r % window);
-    const bool lead = v == 0 && h == 0;
+    const bool lead = v == 0 && h == 0 && layer == 0;  // one error report per row
     const int n = __ldg(num_confirmed + b);
     const int c = __ldg(ctx_lens + b);
     if (n < 0 || n > window || c < 0) {
@@ -112,12 +118,14 @@ __global__ void commit_window_kernel(const S* __restrict__ wk, const S* __restri
       if (lead) set_err(err, MF_ERR_BLOCK_ID);
       continue;
     }
-    const int64_t dst_off =
-        (int64_t)blk * sb + (pos % block_size) * ss + h * sh + (int64_t)v * vec;
-    copy_row_vec<S, P>(wk + r * k_stride_row + h * k_stride_head + (int64_t)v * vec,
-                       key_pool + dst_off, vec);
-    copy_row_vec<S, P>(wv + r * v_stride_row + h * v_stride_head + (int64_t)v * vec,
-                       value_pool + dst_off, vec);
+    const int64_t dst_off = layer * sl + (int64_t)blk * sb + (pos % block_size) * ss + h * sh +
+                            (int64_t)v * vec;
+    copy_row_vec<S, P>(
+        wk + layer * k_stride_layer + r * k_stride_row + h * k_stride_head + (int64_t)v * vec,
+        key_pool + dst_off, vec);
+    copy_row_vec<S, P>(
+        wv + layer * v_stride_layer + r * v_stride_row + h * v_stride_head + (int64_t)v * vec,
+        value_pool + dst_off, vec);
   }
 }
 
@@ -182,28 +190,30 @@ int launch_rac(const void* key, const void* value, int64_t kst, int64_t ksh, int
 }
 
 template <typename S, typename P>
-int launch_commit(const void* wk, const void* wv, int64_t kst, int64_t ksh, int64_t vst,
-                  int64_t vsh, void* kp, void* vp, int64_t sb, int64_t ss, int64_t sh, int32_t nb,
-                  int32_t bs, const int32_t* tables, int32_t table_stride, const int32_t* ctx,
+int launch_commit(const void* wk, const void* wv, int64_t ksl, int64_t kst, int64_t ksh,
+                  int64_t vsl, int64_t vst, int64_t vsh, void* kp, void* vp, int64_t sl,
+                  int64_t sb, int64_t ss, int64_t sh, int L, int32_t nb, int32_t bs,
+                  const int32_t* tables, int32_t table_stride, const int32_t* ctx,
                   const int32_t* conf, int B, int W, int H, int D, int32_t* err,
                   cudaStream_t stream) {
   int vec = 1;
   const int v16 = 16 / (int)sizeof(P);
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  auto al16 = [](int64_t stride, size_t elt) { return (stride * (int64_t)elt) % 16 == 0; };
   if (std::is_same<S, P>::value && D % v16 == 0 && al(wk) && al(wv) && al(kp) && al(vp) &&
-      (kst * sizeof(S)) % 16 == 0 && (ksh * sizeof(S)) % 16 == 0 &&
-      (vst * sizeof(S)) % 16 == 0 && (vsh * sizeof(S)) % 16 == 0 &&
-      (sb * sizeof(P)) % 16 == 0 && (ss * sizeof(P)) % 16 == 0 && (sh * sizeof(P)) % 16 == 0) {
+      al16(ksl, sizeof(S)) && al16(kst, sizeof(S)) && al16(ksh, sizeof(S)) &&
+      al16(vsl, sizeof(S)) && al16(vst, sizeof(S)) && al16(vsh, sizeof(S)) &&
+      al16(sl, sizeof(P)) && al16(sb, sizeof(P)) && al16(ss, sizeof(P)) && al16(sh, sizeof(P))) {
     vec = v16;
   }
-  const int64_t items = (int64_t)B * W * H * (D / vec);
+  const int64_t items = (int64_t)L * B * W * H * (D / vec);
   const int threads = 256;
   int64_t blocks = (items + threads - 1) / threads;
   if (blocks > 148 * 32) blocks = 148 * 32;
   commit_window_kernel<S, P><<<(unsigned)blocks, threads, 0, stream>>>(
-      static_cast<const S*>(wk), static_cast<const S*>(wv), kst, ksh, vst, vsh,
-      static_cast<P*>(kp), static_cast<P*>(vp), sb, ss, sh, nb, bs, tables, table_stride, ctx,
-      conf, B, W, H, D, vec, err);
+      static_cast<const S*>(wk), static_cast<const S*>(wv), ksl, kst, ksh, vsl, vst, vsh,
+      static_cast<P*>(kp), static_cast<P*>(vp), sl, sb, ss, sh, L, nb, bs, tables, table_stride,
+      ctx, conf, B, W, H, D, vec, err);
   return check_launch("commit_window");
 }
 
@@ -270,17 +280,19 @@ extern "C" int mf_copy_blocks(void* key_pool, void* value_pool, int32_t num_laye
 }
 
 extern "C" int mf_commit_window(const void* win_k, const void* win_v, mf_dtype src_dtype,
-                                int64_t k_stride_row, int64_t k_stride_head, int64_t v_stride_row,
-                                int64_t v_stride_head, void* key_pool, void* value_pool,
-                                mf_dtype pool_dtype, int64_t pool_stride_block,
-                                int64_t pool_stride_slot, int64_t pool_stride_head,
-                                int32_t num_blocks, int32_t block_size,
-                                const int32_t* block_tables, int32_t table_stride,
-                                const int32_t* ctx_lens, const int32_t* num_confirmed,
-                                int32_t num_seqs, int32_t window, int32_t num_kv_heads,
-                                int32_t head_dim, int32_t* err_flag, mf_stream_t stream) {
-  if (num_seqs < 0 || window <= 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
-      num_blocks <= 0 || table_stride < 0)
+                                int64_t k_stride_layer, int64_t k_stride_row,
+                                int64_t k_stride_head, int64_t v_stride_layer,
+                                int64_t v_stride_row, int64_t v_stride_head, void* key_pool,
+                                void* value_pool, mf_dtype pool_dtype, int64_t pool_stride_layer,
+                                int64_t pool_stride_block, int64_t pool_stride_slot,
+                                int64_t pool_stride_head, int32_t num_layers, int32_t num_blocks,
+                                int32_t block_size, const int32_t* block_tables,
+                                int32_t table_stride, const int32_t* ctx_lens,
+                                const int32_t* num_confirmed, int32_t num_seqs, int32_t window,
+                                int32_t num_kv_heads, int32_t head_dim, int32_t* err_flag,
+                                mf_stream_t stream) {
+  if (num_seqs < 0 || num_layers <= 0 || window <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      block_size <= 0 || num_blocks <= 0 || table_stride < 0)
     return fail(MF_EINVAL, "commit_window: non-positive size");
   if (num_seqs == 0) return MF_OK;
   if (!win_k || !win_v || !key_pool || !value_pool || !block_tables || !ctx_lens ||
@@ -288,9 +300,10 @@ extern "C" int mf_commit_window(const void* win_k, const void* win_v, mf_dtype s
     return fail(MF_EINVAL, "commit_window: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 #define MF_COMMIT(S, P)                                                                        \
-  return launch_commit<S, P>(win_k, win_v, k_stride_row, k_stride_head, v_stride_row,           \
-                             v_stride_head, key_pool, value_pool, pool_stride_block,            \
-                             pool_stride_slot, pool_stride_head, num_blocks, block_size,        \
+  return launch_commit<S, P>(win_k, win_v, k_stride_layer, k_stride_row, k_stride_head,        \
+                             v_stride_layer, v_stride_row, v_stride_head, key_pool, value_pool, \
+                             pool_stride_layer, pool_stride_block, pool_stride_slot,            \
+                             pool_stride_head, num_layers, num_blocks, block_size,              \
                              block_tables, table_stride, ctx_lens, num_confirmed, num_seqs,     \
                              window, num_kv_heads, head_dim, err_flag, s)
   if (src_dtype == pool_dtype) {

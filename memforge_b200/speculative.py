@@ -71,9 +71,12 @@ def commit_accepted(key_layer: torch.Tensor, value_layer: torch.Tensor, win_k: t
     Write the first ``num_confirmed[b]`` window rows of each sequence into the
     pool: one ``mf_commit_window`` launch (positions ``ctx .. ctx+n-1`` through
     the block table on the device; the rejected rows' slots are left alone).
+    ``key_layer`` is one layer ``(blocks, block_size, H, D)`` with ``(B*W, H, D)``
+    windows, or the whole pool ``(L, blocks, block_size, H, D)`` with
+    ``(L, B*W, H, D)`` windows, which commits every layer in the same launch.
     """
-    if key_layer.shape[1] != block_size:
-        raise ValueError(f"pool block size {key_layer.shape[1]} != {block_size}")
+    if key_layer.shape[-3] != block_size:
+        raise ValueError(f"pool block size {key_layer.shape[-3]} != {block_size}")
     K.commit_window(win_k, win_v, key_layer, value_layer, block_tables, ctx_lens, num_confirmed)
 
 

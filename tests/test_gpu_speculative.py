@@ -158,3 +158,30 @@ def test_commit_window_errors_skip_rows_and_set_bits():
     want_k, _ = _oracle_commit(kp0, vp0, tables, [30, 5, 5, 5],
                                wk, wv, [2, 0, 2, 0], W, "bf16", "bf16")
     assert np.array_equal(_bits(kp), _want_bits(want_k, "bf16"))
+
+
+def test_commit_window_all_layers_in_one_launch():
+    """(L, B*W, H, D) windows into an (L, blocks, 16, H, D) pool: every layer's
+    confirmed rows land, bit-exact, with one launch."""
+    from memforge_b200 import _kernels as K
+    from memforge_b200.speculative import commit_accepted
+    W, L_ = 5, 3
+    ctx = [7, 16, 40, 63]
+    conf = [5, 0, 2, 1]
+    layers = [_commit_case(50 + l, ctx, W) for l in range(L_)]
+    tables = layers[0][2]
+    kp = torch.stack([to_dev(c[0], "bf16") for c in layers])
+    vp = torch.stack([to_dev(c[1], "bf16") for c in layers])
+    wk = torch.stack([to_dev(c[3], "bf16") for c in layers])
+    wv = torch.stack([to_dev(c[4], "bf16") for c in layers])
+    before = K.launch_counter["commit_window"]
+    commit_accepted(kp, vp, wk, wv, torch.from_numpy(tables).cuda(),
+                    torch.tensor(ctx, dtype=torch.int32, device="cuda"),
+                    torch.tensor(conf, dtype=torch.int32, device="cuda"))
+    K.check_device_errors(kp.device)
+    assert K.launch_counter["commit_window"] == before + 1
+    for l, c in enumerate(layers):
+        want_k, want_v = _oracle_commit(c[0], c[1], tables, ctx, c[3], c[4], conf, W, "bf16",
+                                        "bf16")
+        assert np.array_equal(_bits(kp[l]), _want_bits(want_k, "bf16")), l
+        assert np.array_equal(_bits(vp[l]), _want_bits(want_v, "bf16")), l
