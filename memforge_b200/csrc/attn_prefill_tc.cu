@@ -596,18 +596,24 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
             tmem_st32(tO + c * 32, o);
           }
         }
-        // P = 2^(s * scale_log2 - m_ref), packed to 16-bit pairs.
+        // P = 2^(s * scale_log2 - m_ref), packed to 16-bit pairs.  The scaling
+        // and the row sums run as packed fp32 pairs (two columns per
+        // instruction), the exponentials on the SFU.
         const float nmu = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        const uint64_t sl2x2 = f32x2(sl2, sl2), nmux2 = f32x2(nmu, nmu);
+        uint64_t ps2[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
         uint32_t pk[CW / 2];
-        float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < CW / 2; ++c) {
-          const float x0 = fmaf(sv[2 * c], sl2, nmu), x1 = fmaf(sv[2 * c + 1], sl2, nmu);
+          float x0, x1;
+          f32x2_split(f32x2_fma(f32x2(sv[2 * c], sv[2 * c + 1]), sl2x2, nmux2), x0, x1);
           const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          ps[c & 3] += p0 + p1;
+          ps2[c & 1] = f32x2_add(ps2[c & 1], f32x2(p0, p1));
           pk[c] = Mma<T>::pack(p0, p1);
         }
-        l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+        float ps_lo, ps_hi;
+        f32x2_split(f32x2_add(ps2[0], ps2[1]), ps_lo, ps_hi);
+        l_sum += ps_lo + ps_hi;
         // The P buffer is free once the P V product of two tiles ago completed.
         if (g >= 2 && !mbar_wait_bounded(&bar[B_PVDONE + pb], ((g >> 1) - 1) & 1, WAIT_LIMIT))
           ok = false;

@@ -193,6 +193,27 @@ MF_DEVINL float fmax3f(float a, float b, float c) {
   return r;
 }
 
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic: one instruction for both lanes
+// of a 64-bit register pair).
+MF_DEVINL uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+MF_DEVINL void f32x2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+MF_DEVINL uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+MF_DEVINL uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // 2^x on the SFU (the flash-attention formulation works in the log2 domain).
 MF_DEVINL float fast_exp2(float x) {
   float y;
