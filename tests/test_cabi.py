@@ -75,3 +75,21 @@ def test_error_paths_without_a_gpu():
     rc = lib.mf_reshape_and_cache(None, None, 2, 0, 0, 0, 0, None, None, 2, 0, 0, 0, 1, 16,
                                   None, 0, 4, 1, 64, None, None)
     assert rc == L.MF_EINVAL
+
+
+def test_commit_window_validates_before_any_cuda_call():
+    lib = L.lib()
+    # win_k, win_v, src dtype, k/v layer/row/head strides, pools, pool dtype, pool strides,
+    # layers, blocks, block size, tables, table stride, ctx, confirmed, seqs, window, heads, dim
+    def call(src=2, pool=2, layers=1, seqs=2, window=5, heads=8, dim=128, ptr=None):
+        return lib.mf_commit_window(ptr, ptr, src, 0, 0, 0, 0, 0, 0, ptr, ptr, pool, 0, 0, 0, 0,
+                                    layers, 16, 16, ptr, 4, ptr, ptr, seqs, window, heads, dim,
+                                    None, None)
+    assert call(window=0) == L.MF_EINVAL
+    assert call(layers=0) == L.MF_EINVAL
+    assert call() == L.MF_EINVAL and b"null pointer" in lib.mf_last_error()
+    assert call(seqs=0) == L.MF_OK  # nothing to commit
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    assert call(src=L.MF_BF16, pool=L.MF_F32, ptr=p) == L.MF_EUNSUPPORTED
+    assert b"dtype" in lib.mf_last_error()
