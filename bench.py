@@ -2,26 +2,35 @@
 Benchmark of the paged-attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload cfg2|cfg4|cfg5]
+                    [--workload cfg5|cfg2|cfg3|cfg4] [--no-extras]
 
-A step is one pass of the hot path over one batch (BASELINE config 2 by
-default): the KV write of every sequence's new token (reshape_and_cache) and
-single-token paged decode attention over the updated pool, Llama-3-8B shape
-(Hq 32, Hkv 8, D 128, bf16), B = 64 sequences with ctx ~U[256, 4096] on a
-16384-block pool.  The metric is algorithmic HBM bytes per second:
+A step is one pass of the hot path over one batch: the KV write of every
+sequence's new token (reshape_and_cache) and single-token paged decode
+attention over the updated pool.  The default workload is BASELINE config 5,
+the largest single-GPU configuration and the sharded one: Llama-3-70B attention
+(Hq 64, Hkv 8, D 128, bf16), B = 256 sequences with contexts log-uniform in
+[4096, 32768], 14.5 GB of K/V.  The metric is algorithmic HBM bytes per second:
     sum(ctx) * 2 * Hkv * D * 2  (K and V read once per kv head)
   + B * Hq * D * 2 * 2          (Q read, O written)
   + sum(ceil(ctx/16)) * 4       (block table)
   + B * Hkv * D * 2 * 2 * 2 + 4B (new K/V read + written, slot map).
-Inputs (570 MB of KV per step) exceed the 126 MB L2, so no flush is needed.
+The KV read per step exceeds the 126 MB L2, so no flush is needed.
 
-With N GPUs (torchrun, one process per GPU, NCCL) the pool is sharded by kv
-head: each rank holds Hkv/N heads of 64*N sequences (weak scaling: per-GPU
-bytes stay those of N=1), runs the same step on its shard and all-gathers the
-attention outputs with NCCL.  Time is the max over ranks.
+With N GPUs (torchrun, one process per GPU) the pool is split by kv head over
+the SAME sequences (strong scaling): rank r holds kv heads [r*8/N, (r+1)*8/N)
+of all 256 sequences, writes and attends for them, and its decode kernel stores
+its heads' output rows into every rank's output buffer over NVLink (CUDA IPC
+mappings); a bounded flag barrier completes the step.  Time is the max over
+ranks; `value` is the whole step's bytes over that time.
 
-``--impl reference`` times the reference's CPU algorithm (the numpy port in
-oracle/) with all host threads on a bounded sample of the same workload.
+At N = 1 the line also carries BASELINE configs 2, 3 and 4 (`configs`), each
+with its own roofline, a 32-layer config 2 step (`cfg2_32_layers`), the
+reference's own Triton decode kernel timed on the same GPU
+(`reference_gpu_kernel`), and `cpu_baseline`: the reference's CPU path
+(`scatter_kv` + `paged_attention_varlen_materialised` from the installed
+reference, `baseline/_ref`) on a sample of the same workload.
+
+``--impl reference`` times that CPU path alone (rank 0; other ranks exit).
 """
 
 from __future__ import annotations
@@ -41,61 +50,73 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-FALLBACK_HBM_GBS = 6650.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+NOMINAL = {"hbm_gbs": 8000.0, "bf16_tflops": 2250.0}
 BLOCK = 16
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+METRIC = "paged-attn decode HBM GB/s (KV write + decode, algorithmic bytes)"
 
 
-def measured_peaks():
+def measured_peak(key: str):
+    """(peak, 'measured'|'fallback') from MEASURED_PEAKS.json."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return float(d["hbm_gbs"]), "measured"
-    return FALLBACK_HBM_GBS, "fallback"
+        if key in d:
+            return float(d[key]), "measured"
+    return FALLBACK[key], "fallback"
 
 
-# ------------------------------------------------------------------ workload
+def roofline(bound: str, kernel: str, work: float, ms: float, **extra):
+    """Roofline block for one kernel: work per launch (bytes or flops) / launch time."""
+    if bound == "hbm":
+        key, unit, rate = "hbm_gbs", "GB/s", work / (ms * 1e-3) / 1e9
+    else:
+        key, unit, rate = "bf16_tflops", "TFLOP/s", work / (ms * 1e-3) / 1e12
+    peak, src = measured_peak(key)
+    d = {"bound": bound, "kernel": kernel, "achieved": round(rate, 2), "peak": peak,
+         "unit": unit, "frac": round(rate / peak, 4), "peak_source": src,
+         "frac_of_nominal": round(rate / NOMINAL[key], 4), "traffic": None,
+         "kernel_ms": round(ms, 5)}
+    d.update(extra)
+    return d
 
-MODEL_OF = {"cfg2": "Llama-3-8B", "cfg5": "Llama-3-70B", "cfg4": "Qwen2.5-14B"}
+
+# ------------------------------------------------------------------ workloads
+
+MODEL_OF = {"cfg2": "Llama-3-8B", "cfg5": "Llama-3-70B", "cfg4": "Qwen2.5-14B",
+            "cfg3": "Llama-3-8B"}
 
 
-def workload(name: str, world: int):
-    """Host-side metadata of the benchmark workload (identical on every rank)."""
+def decode_workload(name: str):
+    """Host-side metadata of a decode-step workload (identical on every rank)."""
     from tests import cases
     if name == "cfg2":
-        meta = cases.config2_meta(0, batch=64 * world)
-        return dict(name="cfg2", B=64 * world, Hq=32, Hkv=8, D=128, NB=meta["num_blocks"],
-                    ctx=meta["ctx"], tables=meta["tables"], q_per_seq=1, window=False)
+        meta = cases.config2_meta(0)
+        return dict(name="cfg2", B=64, Hq=32, Hkv=8, D=128, NB=meta["num_blocks"],
+                    ctx=meta["ctx"], tables=meta["tables"])
     if name == "cfg5":
         meta = cases.config5_meta(0)
         return dict(name="cfg5", B=256, Hq=64, Hkv=8, D=128, NB=meta["num_blocks"],
-                    ctx=meta["ctx"], tables=meta["tables"], q_per_seq=1, window=False)
-    if name == "cfg4":
-        meta = cases.config4_meta(0)
-        return dict(name="cfg4", B=32, Hq=40, Hkv=8, D=128, NB=meta["num_blocks"],
-                    ctx=meta["ctx"], tables=meta["tables"], q_per_seq=meta["window"],
-                    window=True, accepted=meta["accepted"])
+                    ctx=meta["ctx"], tables=meta["tables"])
     raise ValueError(name)
 
 
-def algorithmic_bytes(w, hkv_local: int, hq_local: int, batch=None):
-    """Bytes one step must move at minimum (see module docstring), per rank."""
-    ctx = w["ctx"] if batch is None else w["ctx"][batch]
+def decode_bytes(ctx: np.ndarray, hkv: int, hq: int, D: int):
+    """(attention bytes, write bytes) one step must move at minimum."""
+    ctx = ctx.astype(np.int64)
     B = len(ctx)
-    D, W = w["D"], w["q_per_seq"]
-    kv_tokens = ctx.astype(np.int64) if not w["window"] else ctx.astype(np.int64)
-    attn = int(kv_tokens.sum()) * 2 * hkv_local * D * 2
-    attn += B * W * hq_local * D * 2 * 2
-    attn += W * B * hkv_local * D * 2 * 2 if w["window"] else 0   # window K/V read
-    attn += int(((kv_tokens + BLOCK - 1) // BLOCK).sum()) * 4 + B * 4
-    write = B * W * hkv_local * D * 2 * 2 * 2 + 4 * B * W
+    attn = int(ctx.sum()) * 2 * hkv * D * 2 + B * hq * D * 2 * 2
+    attn += int(((ctx + BLOCK - 1) // BLOCK).sum()) * 4 + B * 4
+    write = B * hkv * D * 2 * 2 * 2 + 4 * B
     return attn, write
 
 
 # -------------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (median SM MHz, reasons seen)."""
+    """nvidia-smi samples while running (median SM MHz, throttle reasons seen)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -130,7 +151,7 @@ class ClockSampler:
     def summary(self):
         if self.proc is None or not self.path or not os.path.exists(self.path):
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
             for line in f:
@@ -140,6 +161,7 @@ class ClockSampler:
                 try:
                     sm.append(float(parts[1]))
                     mx.append(float(parts[2]))
+                    pw.append(float(parts[3]))
                 except ValueError:
                     continue
                 for n, v in zip(names, parts[5:9]):
@@ -149,240 +171,11 @@ class ClockSampler:
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(pw) if pw else None}
 
 
-# ------------------------------------------------------------- CPU baseline
-
-def cpu_sample_rate(w, k_layer, v_layer, q, seconds: float = 10.0, seqs: int = 8):
-    """
-    The reference's CPU algorithm (numpy port of paged_attention_varlen_
-    materialised + scatter_kv) on a sample of `seqs` sequences, repeated for
-    about `seconds`; returns (GB/s of algorithmic bytes, sample description).
-    """
-    import torch
-    from oracle import paged_oracle as O
-    g = np.random.default_rng(1)
-    pick = np.sort(g.choice(len(w["ctx"]), size=min(seqs, len(w["ctx"])), replace=False))
-    ctx = w["ctx"][pick]
-    tables = w["tables"][pick]
-    used = np.unique(np.concatenate([tables[i][: (int(c) + BLOCK - 1) // BLOCK]
-                                     for i, c in enumerate(ctx)]))
-    remap = {int(b): i for i, b in enumerate(used)}
-    idx = torch.from_numpy(used.astype(np.int64)).to(k_layer.device)
-    kp = k_layer.index_select(0, idx).float().cpu().numpy()
-    vp = v_layer.index_select(0, idx).float().cpu().numpy()
-    qs = q.view(len(w["ctx"]), -1, w["Hq"], w["D"])[torch.from_numpy(pick).to(q.device)]
-    qs = qs.float().cpu().numpy().reshape(-1, w["Hq"], w["D"])
-    tabs = [np.array([remap[int(b)] for b in tables[i][: (int(c) + BLOCK - 1) // BLOCK]])
-            for i, c in enumerate(ctx)]
-    W = w["q_per_seq"]
-    seq_ids = [s for s in range(len(pick)) for _ in range(W)]
-    positions = [int(ctx[s]) - W + j for s in range(len(pick)) for j in range(W)]
-    new_k = np.zeros((1, w["Hkv"], len(pick), w["D"]), np.float32)
-    flat = np.array([tabs[s][(int(ctx[s]) - 1) // BLOCK] * BLOCK + (int(ctx[s]) - 1) % BLOCK
-                     for s in range(len(pick))])
-    attn_b, write_b = algorithmic_bytes(w, w["Hkv"], w["Hq"], batch=pick)
-    qh = np.ascontiguousarray(np.transpose(qs, (1, 0, 2)))
-    n, t0 = 0, time.perf_counter()
-    while True:
-        O.scatter_kv(kp[None], vp[None], 0, flat, new_k, new_k, "f32", "f32")
-        O.varlen_attention(qh, kp[None], vp[None], 0, tabs, seq_ids, positions, BLOCK,
-                           scale=1.0 / math.sqrt(w["D"]))
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds or n >= 200:
-            break
-    rate = (attn_b + write_b) * n / el / 1e9
-    return rate, f"{len(pick)} of {len(w['ctx'])} sequences (sum ctx {int(ctx.sum())}), {n} passes in {el:.1f} s"
-
-
-# ---------------------------------------------------------------- our arm
-
-def run_ours(args):
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    from memforge_b200 import _kernels as K
-    from memforge_b200.build import build
-    if rank == 0 and not os.path.exists(os.path.join(ROOT, "memforge_b200", "libmemforge_sm100.so")):
-        build()
-    if world > 1:
-        dist.barrier()
-
-    w = workload(args.workload, world)
-    if w["Hkv"] % world:
-        raise SystemExit(f"{w['Hkv']} kv heads do not shard over {world} GPUs")
-    hkv = w["Hkv"] // world
-    hq = w["Hq"] // world
-    B, D, NB, W = w["B"], w["D"], w["NB"], w["q_per_seq"]
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    kp = torch.randn((NB, BLOCK, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    vp = torch.randn((NB, BLOCK, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    q = torch.randn((B * W, hq, D), generator=g, device=dev, dtype=torch.bfloat16)
-    new_k = torch.randn((B * W, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    new_v = torch.randn((B * W, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    tables = torch.from_numpy(w["tables"].clip(min=0).astype(np.int32)).to(dev)
-    ctx = torch.from_numpy(w["ctx"].astype(np.int32)).to(dev)
-    pos = w["ctx"].astype(np.int64) - 1
-    slots_np = (w["tables"][np.arange(B), pos // BLOCK].astype(np.int64) * BLOCK + pos % BLOCK)
-    slots = torch.from_numpy(slots_np.astype(np.int32)).to(dev)
-    out = torch.empty((B * W, hq, D), device=dev, dtype=torch.bfloat16)
-    scale = 1.0 / math.sqrt(D)
-    # N > 1: the full [B, Hq, D] output is assembled over peer memory: every
-    # rank's decode kernel stores its heads into all ranks' output buffers
-    # (two, alternating per step) and a flag barrier completes the step.
-    peer = None
-    if world > 1:
-        from memforge_b200.kv_shard import PeerOutput
-        peer = PeerOutput(B * W, hq * world, D, torch.bfloat16, dev)
-
-    def write():
-        K.reshape_and_cache(new_k, new_v, kp, vp, slots)
-
-    def attend(buf=None):
-        if peer is None:
-            K.paged_attention(q, out, kp, vp, tables, ctx, q_per_seq=1, scale=scale, causal=True)
-        else:
-            K.paged_attention(q, peer.outs[buf], kp, vp, tables, ctx, q_per_seq=1, scale=scale,
-                              causal=True, out_peers=peer.pointers(buf),
-                              out_head_offset=rank * hq)
-
-    def collective():
-        if peer is not None:
-            peer.barrier()
-
-    stream = torch.cuda.current_stream(dev)
-    for _ in range(max(3, args.warmup)):
-        write()
-        attend(None if peer is None else peer.current)
-        collective()
-    torch.cuda.synchronize(dev)
-    K.check_device_errors(dev)
-    # The step (KV write, then attention: a programmatic dependent launch lets the
-    # attention start while the write finishes) is captured once in a CUDA graph
-    # and replayed every step, the way MemForge's graphed decode runs, so host
-    # launch cost stays off the device timeline.  With peer output there is one
-    # graph per output buffer.  Separate graphs of each kernel alone are timed
-    # with CUDA events for the roofline.
-    nbuf = 1 if peer is None else len(peer.outs)
-    g_steps = [capture_graph(lambda b=b: (write(), attend(None if peer is None else b)), dev)
-               for b in range(nbuf)]
-    n_step = g_steps[0][1]
-    g_write, _ = capture_graph(write, dev)
-    g_attns = [capture_graph(lambda b=b: attend(None if peer is None else b), dev)
-               for b in range(nbuf)]
-
-    def cur():
-        return 0 if peer is None else peer.current
-
-    for _ in range(max(3, args.warmup)):
-        g_steps[cur()][0].replay()
-        collective()
-    torch.cuda.synchronize(dev)
-    K.check_device_errors(dev)
-
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clk:
-        start_all = torch.cuda.Event(enable_timing=True)
-        end_all = torch.cuda.Event(enable_timing=True)
-        start_all.record(stream)
-        for i in range(args.steps):
-            g_steps[cur()][0].replay()
-            collective()
-        end_all.record(stream)
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    total_ms = start_all.elapsed_time(end_all)
-    kernel_launches = (n_step + (1 if peer is not None else 0)) * args.steps
-    K.check_device_errors(dev)
-
-    # Each kernel alone, CUDA events around every launch, same steps count.
-    def per_launch(graphs):
-        ms = []
-        for i in range(args.steps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            graphs[i % len(graphs)][0].replay()
-            b.record(stream)
-            ms.append((a, b))
-        torch.cuda.synchronize(dev)
-        return [a.elapsed_time(b) for a, b in ms]
-    write_ms = per_launch([(g_write, 0)])
-    decode_ms = per_launch(g_attns)
-    if world > 1:
-        dist.barrier()
-
-    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_step = float(t.item()) / args.steps
-    attn_b, write_b = algorithmic_bytes(w, hkv, hq)
-    step_bytes_all = (attn_b + write_b) * world
-    value = step_bytes_all / (ms_step * 1e-3) / 1e9
-    dec_ms = statistics.mean(decode_ms)
-    peak, peak_kind = measured_peaks()
-    achieved = attn_b / (dec_ms * 1e-3) / 1e9
-
-    # ------------------------------------------------ end-to-end (host buffers)
-    e2e = run_e2e(args, w, dev, kp, vp, hkv, hq, world, peer, rank)
-
-    res = None
-    if rank == 0:
-        res = {
-            "metric": "paged-attn decode HBM GB/s (KV write + decode, algorithmic bytes)",
-            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (seeded; random-init pool)",
-            "config": {"workload": f"BASELINE {w['name']}: KV write + decode, "
-                                   f"{MODEL_OF.get(w['name'], '')} attention "
-                                   f"(Hq {w['Hq']}, Hkv {w['Hkv']}, D {w['D']}), block 16",
-                       "batch": B, "kv_heads_per_gpu": hkv, "sum_ctx": int(w["ctx"].sum()),
-                       "pool_blocks": NB, "parallelism": f"kv-head shard x{world}" if world > 1 else "1 GPU",
-                       "l2": "inputs exceed L2 (KV read per step > 126 MB); no flush",
-                       "launch": "the step (KV write, then decode as a programmatic dependent launch) captured once as one CUDA graph, replayed every step"},
-            "attn_tokens_per_s": round(B * W * world / (ms_step * 1e-3), 1) if world == 1 else round(B * W / (ms_step * 1e-3), 1),
-            "roofline": {"bound": "hbm", "kernel": "paged decode (tc::decode_kernel)",
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "frac_of_nominal_8TBs": round(achieved / 8000.0, 4),
-                         "traffic": TRAFFIC_BYTES.get(w["name"]) if world == 1 else None,
-                         "algorithmic_bytes": attn_b, "kernel_ms": round(dec_ms, 5),
-                         "write_kernel_ms": round(statistics.mean(write_ms), 5)},
-            "e2e": e2e, "gpu_launches": kernel_launches,
-            "clocks": clk.summary(),
-        }
-        if world == 1 and not args.no_cpu_baseline:
-            rate, sample = cpu_sample_rate(w, kp, vp, q, seconds=args.cpu_seconds)
-            res["cpu_baseline"] = {"value": round(rate, 3), "unit": "GB/s",
-                                   "cores": os.cpu_count(), "kind": "port",
-                                   "sample": sample}
-        print(json.dumps(res), flush=True)
-    if world > 1:
-        del g_attns, g_steps
-        peer.close()
-        dist.barrier()
-        dist.destroy_process_group()
-    return res
-
-
-# Per-launch DRAM bytes (read + write) of the decode kernel at this workload from
-# one ncu capture (profiles/decode_cfg2.md: 583.214 MB read + 6.235 MB written).
-TRAFFIC_BYTES = {"cfg2": 589448704}
-
+# ------------------------------------------------------------ CUDA helpers
 
 def capture_graph(fn, dev):
     """(CUDA graph replaying fn, launches of this library's kernels per replay)."""
@@ -402,158 +195,513 @@ def capture_graph(fn, dev):
     return g, sum(K.launch_counter.values()) - before
 
 
-def run_e2e(args, w, dev, kp, vp, hkv, hq, world, peer=None, rank=0):
+def events_ms(pairs):
+    return [a.elapsed_time(b) for a, b in pairs]
+
+
+def max_over_ranks(x: float, dev, world: int) -> float:
+    import torch
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def close_enough(got, want):
+    """bf16 tolerance of the path: |got - want| <= 2e-2 + 1e-2 |want|."""
+    g, w = got.float(), want.float()
+    err = (g - w).abs()
+    ok = bool((err <= 2e-2 + 1e-2 * w.abs()).all()) and bool(g.isfinite().all())
+    return ok, float(err.max())
+
+
+# ------------------------------------------------------- decode-step state
+
+class DecodeStep:
+    """One rank's share of a decode-step workload: pool shard, inputs, graphs."""
+
+    def __init__(self, w, world: int, rank: int, dev, layers: int = 1):
+        import torch
+        from memforge_b200 import _kernels as K
+        self.K, self.w, self.world, self.rank, self.dev = K, w, world, rank, dev
+        if w["Hkv"] % world:
+            raise SystemExit(f"{w['Hkv']} kv heads do not shard over {world} GPUs")
+        self.hkv, self.hq = w["Hkv"] // world, w["Hq"] // world
+        B, D, NB = w["B"], w["D"], w["NB"]
+        self.layers = layers
+        g = torch.Generator(device=dev).manual_seed(1000 + rank)
+        shape = (layers, NB, BLOCK, self.hkv, D)
+        self.kp = torch.randn(shape, generator=g, device=dev, dtype=torch.bfloat16)
+        self.vp = torch.randn(shape, generator=g, device=dev, dtype=torch.bfloat16)
+        self.q = torch.randn((B, self.hq, D), generator=g, device=dev, dtype=torch.bfloat16)
+        self.new_k = torch.randn((B, self.hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+        self.new_v = torch.randn((B, self.hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+        self.tables = torch.from_numpy(w["tables"].clip(min=0).astype(np.int32)).to(dev)
+        self.ctx = torch.from_numpy(w["ctx"].astype(np.int32)).to(dev)
+        pos = w["ctx"].astype(np.int64) - 1
+        slots = w["tables"][np.arange(B), pos // BLOCK].astype(np.int64) * BLOCK + pos % BLOCK
+        self.slots = torch.from_numpy(slots.astype(np.int32)).to(dev)
+        self.out = torch.empty((B, self.hq, D), device=dev, dtype=torch.bfloat16)
+        self.scale = 1.0 / math.sqrt(D)
+        self.peer = None
+        if world > 1:
+            from memforge_b200.kv_shard import PeerOutput
+            self.peer = PeerOutput(B, w["Hq"], D, torch.bfloat16, dev)
+
+    def write(self, layer=0):
+        self.K.reshape_and_cache(self.new_k, self.new_v, self.kp[layer], self.vp[layer],
+                                 self.slots)
+
+    def attend(self, buf=None, layer=0):
+        K = self.K
+        if self.peer is None:
+            K.paged_attention(self.q, self.out, self.kp[layer], self.vp[layer], self.tables,
+                              self.ctx, q_per_seq=1, scale=self.scale, causal=True)
+        else:
+            K.paged_attention(self.q, self.peer.outs[buf], self.kp[layer], self.vp[layer],
+                              self.tables, self.ctx, q_per_seq=1, scale=self.scale,
+                              causal=True, out_peers=self.peer.pointers(buf),
+                              out_head_offset=self.rank * self.hq)
+
+    def result(self, buf=None):
+        """This rank's heads of the last output, [B, hq, D]."""
+        if self.peer is None:
+            return self.out
+        a = self.rank * self.hq
+        return self.peer.outs[buf][:, a:a + self.hq]
+
+    def collective(self):
+        if self.peer is not None:
+            self.peer.barrier()
+
+    def current(self):
+        return 0 if self.peer is None else self.peer.current
+
+    def nbuf(self):
+        return 1 if self.peer is None else len(self.peer.outs)
+
+    def validate(self, buf, picks):
+        """Sampled sequences of the last output against the fp32 torch reference."""
+        from tests.gpu_util import torch_reference
+        worst, ok = 0.0, True
+        for s in picks:
+            want = torch_reference(self.q[s:s + 1], self.kp[0], self.vp[0], self.tables[s:s + 1],
+                                   self.w["ctx"][s:s + 1], [1], self.scale)
+            good, err = close_enough(self.result(buf)[s:s + 1], want)
+            ok, worst = ok and good, max(worst, err)
+        return ok, worst
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+
+
+def sample_sequences(w, n: int, seed: int = 5):
+    g = np.random.default_rng(seed)
+    B = len(w["ctx"])
+    pick = set(g.choice(B, size=min(n, B), replace=False).tolist())
+    pick |= {int(np.argmin(w["ctx"])), int(np.argmax(w["ctx"]))}
+    return sorted(pick)
+
+
+def bench_decode_step(args, w, world, rank, local, dev, with_clocks: bool):
     """
-    Same step through the reference-facing API with HOST inputs: every step
-    copies q, new K/V, slot map, block tables and lengths from pinned host
-    memory, runs scatter_kv + paged_decode_attention, and reads the output back
-    to pinned host memory.  The device part of the step is one CUDA graph
-    (copies and kernels), as in MemForge's graphed decode.  At N > 1 the
-    attention stores its heads into every rank's output over peer memory
-    (kv_shard.PeerOutput, one graph per output buffer), the peer barrier
-    completes the step and the full output is read back.
+    Time K decode steps of workload w on this rank.  The step is two CUDA graphs
+    (the KV write, then the decode; with N > 1 one decode graph per peer output
+    buffer) plus, with N > 1, the peer barrier.  CUDA events on the launching
+    stream bracket each step and the decode graph inside it, so the roofline's
+    kernel time comes from the timed region itself.
     """
     import torch
-    from memforge_b200.paged_decode import paged_decode_attention
-    from memforge_b200 import _kernels as K
-    B, D, W = w["B"], w["D"], w["q_per_seq"]
-    g = torch.Generator().manual_seed(7)
-    h_q = torch.randn((B, hq, D), generator=g).to(torch.bfloat16).pin_memory()
-    h_k = torch.randn((B, hkv, D), generator=g).to(torch.bfloat16).pin_memory()
-    h_v = torch.randn((B, hkv, D), generator=g).to(torch.bfloat16).pin_memory()
-    pos = w["ctx"].astype(np.int64) - 1
-    h_slots = torch.from_numpy((w["tables"][np.arange(B), pos // BLOCK].astype(np.int64) * BLOCK
-                                + pos % BLOCK).astype(np.int32)).pin_memory()
-    h_tab = torch.from_numpy(w["tables"].clip(min=0).astype(np.int32)).pin_memory()
-    h_ctx = torch.from_numpy(w["ctx"].astype(np.int32)).pin_memory()
-    h_out = torch.empty((B, hq * world, D), dtype=torch.bfloat16).pin_memory()
-    scale = 1.0 / math.sqrt(D)
+    import torch.distributed as dist
+    st = DecodeStep(w, world, rank, dev)
+    K = st.K
     stream = torch.cuda.current_stream(dev)
-    # The step's host inputs sit in one pinned staging buffer, so each step
-    # makes one host-to-device copy (and one device-to-host read of the output).
-    hosts = (h_q, h_k, h_v, h_slots, h_tab, h_ctx)
+    for _ in range(max(3, args.warmup)):
+        st.write()
+        st.attend(None if st.peer is None else st.current())
+        st.collective()
+    torch.cuda.synchronize(dev)
+    K.check_device_errors(dev)
+
+    # Self-check before timing: sampled sequences against the fp32 reference.
+    st.write()
+    b = st.current()
+    st.attend(b if st.peer else None)
+    st.collective()
+    torch.cuda.synchronize(dev)
+    picks = sample_sequences(w, 4)
+    ok, worst = st.validate(b if st.peer else None, picks)
+    okv = max_over_ranks(0.0 if ok else 1.0, dev, world) == 0.0
+    if not okv:
+        raise SystemExit(f"bench self-check failed on {w['name']}: max |err| {worst:.3e}")
+    validated = {"sequences": picks, "ranks": world, "max_abs_err": round(worst, 5),
+                 "tolerance": "2e-2 abs + 1e-2 rel vs fp32 torch reference", "ok": True}
+
+    g_write, n_write = capture_graph(st.write, dev)
+    g_dec = [capture_graph(lambda b=b: st.attend(None if st.peer is None else b), dev)
+             for b in range(st.nbuf())]
+    n_dec = g_dec[0][1]
+    for _ in range(max(3, args.warmup)):
+        g_write.replay()
+        g_dec[st.current()][0].replay()
+        st.collective()
+    torch.cuda.synchronize(dev)
+    K.check_device_errors(dev)
+
+    def run(n, evs=None):
+        for i in range(n):
+            if evs is not None:
+                evs[i][0].record(stream)
+            g_write.replay()
+            if evs is not None:
+                evs[i][1].record(stream)
+            g_dec[st.current()][0].replay()
+            if evs is not None:
+                evs[i][2].record(stream)
+            st.collective()
+            if evs is not None:
+                evs[i][3].record(stream)
+
+    # Clock soak: >= soak_seconds of the same replays under the sampler before
+    # the timed steps, so the clock record covers seconds of real load.
+    est = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    est[0].record(stream)
+    run(5)
+    est[1].record(stream)
+    torch.cuda.synchronize(dev)
+    per = max(est[0].elapsed_time(est[1]) / 5, 1e-3)
+    soak_n = int(max_over_ranks(math.ceil(args.soak_seconds * 1e3 / per), dev, world))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clk = ClockSampler(local) if with_clocks else None
+    if clk:
+        clk.__enter__()
+    try:
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        run(soak_n)
+        s1.record(stream)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+               for _ in range(args.steps)]
+        if world > 1:
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        run(args.steps, evs)
+        torch.cuda.synchronize(dev)
+    finally:
+        if clk:
+            clk.__exit__(None, None, None)
+    if world > 1:
+        dist.barrier()
+    K.check_device_errors(dev)
+    total_ms = evs[0][0].elapsed_time(evs[-1][3])
+    dec_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in evs)
+    wr_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in evs)
+    ms_step = max_over_ranks(total_ms, dev, world) / args.steps
+    soak_ms = s0.elapsed_time(s1)
+    attn_b, write_b = decode_bytes(w["ctx"], st.hkv, st.hq, w["D"])
+    launches = (n_write + n_dec + (1 if st.peer is not None else 0)) * args.steps
+    res = {
+        "ms_per_step": ms_step, "value": (attn_b + write_b) * world / (ms_step * 1e-3) / 1e9,
+        "roofline": roofline("hbm", "paged decode (tc::decode_kernel), this rank's heads",
+                             attn_b, dec_ms, algorithmic_bytes=attn_b,
+                             write_kernel_ms=round(wr_ms, 5)),
+        "launches": launches, "validated": validated,
+        "soak": {"seconds": round(soak_ms / 1e3, 3), "replays": soak_n,
+                 "ms_per_step": round(soak_ms / max(soak_n, 1), 5)},
+        "clocks": clk.summary() if clk else None,
+    }
+    return st, res
+
+
+# -------------------------------------------------------------- end to end
+
+def run_e2e(args, st, world, rank, dev):
+    """
+    The same step through the public API with HOST buffers.  Every step copies
+    that step's inputs (q, new K/V, slot map, context lengths and the block-table
+    entries of pages opened this step) from pinned host memory, runs the KV
+    write (paged_gather.scatter_kv) and decode (paged_decode.paged_decode_attention;
+    with N > 1 the head-sharded decode storing into every rank's output plus the
+    peer barrier), and reads the output back to pinned host memory (rank 0, the
+    full [B, Hq, D]).  Copies run on a copy stream, triple-buffered, so step
+    i+1's upload and step i's read-back overlap the kernels of step i.  The
+    block tables stay resident on the device; only new page entries travel.
+    """
+    import torch
+    from memforge_b200.kv_shard import PeerOutput
+    from memforge_b200.paged_decode import paged_decode_attention
+    from memforge_b200.paged_gather import scatter_kv
+    w = st.w
+    B, D, hq, hkv = w["B"], w["D"], st.hq, st.hkv
+    NBUF = 3
+    g = torch.Generator().manual_seed(7 + rank)
+    pos = w["ctx"].astype(np.int64) - 1
+    opened = np.nonzero(pos % BLOCK == 0)[0]          # sequences whose new token opens a page
+    delta = np.stack([opened, pos[opened] // BLOCK,
+                      w["tables"][opened, pos[opened] // BLOCK]], 1).astype(np.int32)
+    slots = (w["tables"][np.arange(B), pos // BLOCK].astype(np.int64) * BLOCK + pos % BLOCK)
+    host = [torch.randn((B, hq, D), generator=g).to(torch.bfloat16),
+            torch.randn((1, hkv, B, D), generator=g).to(torch.bfloat16),
+            torch.randn((1, hkv, B, D), generator=g).to(torch.bfloat16),
+            torch.from_numpy(slots.astype(np.int64)),
+            torch.from_numpy(w["ctx"].astype(np.int32)),
+            torch.from_numpy(delta.reshape(-1, 3) if len(delta) else np.zeros((0, 3), np.int32))]
     offs, total = [], 0
-    for t in hosts:
+    for t in host:
         offs.append(total)
         total += (t.numel() * t.element_size() + 255) // 256 * 256
-    h_all = torch.empty(total, dtype=torch.uint8).pin_memory()
-    d_all = torch.empty(total, dtype=torch.uint8, device=dev)
+    total = max(total, 256)
+    h_stage = [torch.empty(total, dtype=torch.uint8).pin_memory() for _ in range(NBUF)]
+    d_stage = [torch.empty(total, dtype=torch.uint8, device=dev) for _ in range(NBUF)]
 
     def carve(buf, t, off):
         return buf[off:off + t.numel() * t.element_size()].view(t.dtype).view(t.shape)
-    for t, off in zip(hosts, offs):
-        carve(h_all, t, off).copy_(t)
-    d_in = [carve(d_all, t, off) for t, off in zip(hosts, offs)]
-    res = {}
+    for hs in h_stage:
+        for t, off in zip(host, offs):
+            carve(hs, t, off).copy_(t)
+    # The device staging holds valid inputs before the graphs' eager warm-up
+    # runs on it (the timed steps then refresh it from the host every step).
+    for hs, ds in zip(h_stage, d_stage):
+        ds.copy_(hs)
+    torch.cuda.synchronize(dev)
+    d_in = [[carve(ds, t, off) for t, off in zip(host, offs)] for ds in d_stage]
+    tables = st.tables.clone()
+    key_flat = [st.kp[0].view(-1, hkv, D)]
+    value_flat = [st.vp[0].view(-1, hkv, D)]
+    max_ctx = int(w["ctx"].max())
+    peer = PeerOutput(B, w["Hq"], D, torch.bfloat16, dev, buffers=NBUF) if world > 1 else None
+    outs = [torch.empty((B, hq, D), dtype=torch.bfloat16, device=dev) for _ in range(NBUF)] \
+        if peer is None else peer.outs
+    h_out = [torch.empty((B, w["Hq"], D), dtype=torch.bfloat16).pin_memory()
+             for _ in range(NBUF)]
+    reads_back = rank == 0
 
-    def device_part(buf=None):
-        d_all.copy_(h_all, non_blocking=True)
-        q, k, v, sl, tab, cx = d_in
-        K.reshape_and_cache(k, v, kp, vp, sl)
-        if world == 1:
-            res["o"] = paged_decode_attention(q, kp.view(-1, hkv, D), vp.view(-1, hkv, D), tab,
-                                              cx, BLOCK, int(w["ctx"].max()), scale)
-            h_out.copy_(res["o"], non_blocking=True)
+    def device_part(b):
+        q, k, v, sl, cx, dl = d_in[b]
+        if dl.shape[0]:
+            tables.index_put_((dl[:, 0].long(), dl[:, 1].long()), dl[:, 2])
+        scatter_kv(st.kp, st.vp, 0, sl, k, v, BLOCK)
+        if peer is None:
+            paged_decode_attention(q, key_flat[0], value_flat[0], tables, cx, BLOCK, max_ctx,
+                                   st.scale, out=outs[b])
         else:
-            K.paged_attention(q, peer.outs[buf], kp, vp, tab, cx, q_per_seq=1, scale=scale,
-                              causal=True, out_peers=peer.pointers(buf),
-                              out_head_offset=rank * hq)
+            st.K.paged_attention(q, peer.outs[b], st.kp[0], st.vp[0], tables, cx, q_per_seq=1,
+                                 scale=st.scale, causal=True, out_peers=peer.pointers(b),
+                                 out_head_offset=rank * hq)
 
-    def tail():
-        if world > 1:
-            h_out.copy_(peer.barrier(), non_blocking=True)
+    graphs = [capture_graph(lambda b=b: device_part(b), dev)[0] for b in range(NBUF)]
+    s = torch.cuda.current_stream(dev)
+    cs = torch.cuda.Stream(dev)
+    ev = {k: [torch.cuda.Event() for _ in range(NBUF)] for k in ("h2d", "done", "d2h")}
 
-    def timed(step):
-        for _ in range(3):
-            step()
+    def idx(i, e0):
+        return (e0 + 1 + i) % NBUF
+
+    def steps(n):
+        e0 = peer.epoch if peer is not None else -1
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(s)
+        cs.wait_stream(s)
+        with torch.cuda.stream(cs):
+            b = idx(0, e0)
+            d_stage[b].copy_(h_stage[b], non_blocking=True)
+            ev["h2d"][b].record(cs)
+        for i in range(n):
+            b = idx(i, e0)
+            s.wait_event(ev["h2d"][b])
+            if i >= 2:
+                s.wait_event(ev["d2h"][idx(i - 2, e0)])
+            graphs[b].replay()
+            if peer is not None:
+                assert peer.current == b
+                peer.barrier()
+            ev["done"][b].record(s)
+            with torch.cuda.stream(cs):
+                if i + 1 < n:
+                    nb = idx(i + 1, e0)
+                    if i + 1 >= NBUF:
+                        cs.wait_event(ev["done"][nb])
+                    d_stage[nb].copy_(h_stage[nb], non_blocking=True)
+                    ev["h2d"][nb].record(cs)
+                cs.wait_event(ev["done"][b])
+                if reads_back:
+                    h_out[b].copy_(outs[b] if peer is None else peer.outs[b], non_blocking=True)
+                ev["d2h"][b].record(cs)
+        s.wait_event(ev["d2h"][idx(n - 1, e0)])
+        t1.record(s)
         torch.cuda.synchronize(dev)
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        for _ in range(args.steps):
-            step()
-        e.record(stream)
-        torch.cuda.synchronize(dev)
-        t = torch.tensor([s.elapsed_time(e) / args.steps], device=dev, dtype=torch.float64)
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return t0.elapsed_time(t1) / n
 
-    if world == 1:
-        eager_ms = timed(lambda: (device_part(), tail()))
-        g, _ = capture_graph(device_part, dev)
-        ms = timed(lambda: (g.replay(), tail()))
-    else:
-        eager_ms = timed(lambda: (device_part(peer.current), tail()))
-        gs = [capture_graph(lambda b=b: device_part(b), dev)[0] for b in range(len(peer.outs))]
-        ms = timed(lambda: (gs[peer.current].replay(), tail()))
-        g = gs
-    attn_b, write_b = algorithmic_bytes(w, hkv, hq)
-    bi = h_all.numel()
-    bo = h_out.numel() * h_out.element_size()
-    del g
-    return {"value": round((attn_b + write_b) * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(ms, 5), "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
-            "eager_value": round((attn_b + write_b) * world / (eager_ms * 1e-3) / 1e9, 2),
-            "eager_ms_per_step": round(eager_ms, 5),
-            "api": ("memforge_b200 reshape_and_cache + paged_decode_attention, pinned host "
-                    "buffers; H2D copies + kernels + D2H replayed as one CUDA graph")
-                   if world == 1 else
-                   ("memforge_b200 reshape_and_cache + paged attention storing its heads into "
-                    "every rank's output (kv_shard.PeerOutput) + peer barrier, pinned host "
-                    "buffers; H2D copies + kernels replayed as CUDA graphs, full output read back")}
+    steps(max(3, args.warmup))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    ms = max_over_ranks(steps(args.steps), dev, world)
+    st.K.check_device_errors(dev)
+    attn_b, write_b = decode_bytes(w["ctx"], hkv, hq, D)
+    step_bytes = (attn_b + write_b) * world
+    h2d = total * world
+    d2h = B * w["Hq"] * D * 2
+    del graphs
+    if peer is not None:
+        peer.close()
+    return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "table_entries_sent_per_step": int(len(delta)),
+            "api": ("memforge_b200.paged_gather.scatter_kv + paged_decode.paged_decode_attention"
+                    if world == 1 else
+                    "memforge_b200 reshape_and_cache + head-sharded paged attention storing into "
+                    "every rank's output (kv_shard.PeerOutput) + peer barrier") +
+                   "; pinned host staging, H2D / D2H on a copy stream overlapping the kernels, "
+                   "device-resident block tables updated with the step's new page entries; "
+                   f"h2d counts all {world} rank(s), d2h is rank 0's read of the full output"}
 
 
-# ----------------------------------------------------------- reference arm
+# ------------------------------------------------ reference CPU path (timed)
+
+def _reference_modules():
+    """The installed reference's CPU functions, or None when it is absent."""
+    if not os.path.isdir(os.path.join(REF_DIR, "memforge_ml")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from memforge_ml.kernels import paged_gather as PG
+        from memforge_ml.kernels import varlen_attention as VA
+        from memforge_ml.runtime.kv_pool import ModelKVSpec, PagedKVPool
+    except Exception:
+        return None
+    return PG, VA, ModelKVSpec, PagedKVPool
+
+
+class ReferenceCPU:
+    """
+    The reference's own CPU path for a decode step (``scatter_kv`` +
+    ``paged_attention_varlen_materialised``, imported from the installed
+    reference) on a sample of the workload's sequences, with all host threads.
+    Falls back to the numpy port in oracle/ when the reference is not installed.
+    """
+
+    def __init__(self, w, picks):
+        import torch
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.w, self.picks = w, list(picks)
+        self.mods = _reference_modules()
+        self.kind = "reference" if self.mods else "port"
+        D, Hkv, Hq = w["D"], w["Hkv"], w["Hq"]
+        ctx = w["ctx"][self.picks]
+        self.ctx = ctx
+        nblk = [(int(c) + BLOCK - 1) // BLOCK for c in ctx]
+        NB = sum(nblk)
+        g = torch.Generator().manual_seed(3)
+        at, self.tabs = 0, []
+        for n in nblk:
+            self.tabs.append(torch.arange(at, at + n, dtype=torch.int64))
+            at += n
+        kp = torch.randn((1, NB, BLOCK, Hkv, D), generator=g).to(torch.bfloat16)
+        vp = torch.randn((1, NB, BLOCK, Hkv, D), generator=g).to(torch.bfloat16)
+        self.q = torch.randn((1, Hq, len(ctx), D), generator=g).to(torch.bfloat16)
+        self.nk = torch.randn((1, Hkv, len(ctx), D), generator=g).to(torch.bfloat16)
+        self.flat = torch.tensor([int(self.tabs[s][(int(c) - 1) // BLOCK]) * BLOCK
+                                  + (int(c) - 1) % BLOCK for s, c in enumerate(ctx)])
+        if self.mods:
+            PG, VA, Spec, Pool = self.mods
+            self.pool = Pool(Spec(num_layers=1, num_kv_heads=Hkv, head_dim=D,
+                                  dtype=torch.bfloat16, device="cpu"), num_blocks=NB,
+                             block_size=BLOCK)
+            self.pool.key_pool.copy_(kp)
+            self.pool.value_pool.copy_(vp)
+        else:
+            self.np_k, self.np_v = kp.float().numpy(), vp.float().numpy()
+            self.np_q = self.q[0].float().numpy()
+            self.np_nk = self.nk.float().numpy()
+
+    def step(self, s: int):
+        """One decode step of sampled sequence s (its KV write, then attention)."""
+        c = int(self.ctx[s])
+        if self.mods:
+            PG, VA, _, _ = self.mods
+            PG.scatter_kv(self.pool.key_pool, self.pool.value_pool, 0, self.flat[s:s + 1],
+                          self.nk[:, :, s:s + 1], self.nk[:, :, s:s + 1], BLOCK)
+            VA.paged_attention_varlen_materialised(self.q[:, :, s:s + 1], self.pool, 0,
+                                                   [self.tabs[s]], [0], [c - 1])
+        else:
+            from oracle import paged_oracle as O
+            O.scatter_kv(self.np_k, self.np_v, 0, self.flat[s:s + 1].numpy(),
+                         self.np_nk[:, :, s:s + 1], self.np_nk[:, :, s:s + 1], "f32", "f32")
+            O.varlen_attention(self.np_q[:, s:s + 1], self.np_k, self.np_v, 0,
+                               [self.tabs[s].numpy()], [0], [c - 1], BLOCK,
+                               scale=1.0 / math.sqrt(self.w["D"]))
+
+    def bytes_of(self, s: int) -> int:
+        a, b = decode_bytes(self.ctx[s:s + 1], self.w["Hkv"], self.w["Hq"], self.w["D"])
+        return a + b
+
+    def describe(self, n_steps: int) -> str:
+        what = ("the installed reference's scatter_kv + paged_attention_varlen_materialised "
+                "(torch CPU, bf16 pool)" if self.kind == "reference" else
+                "numpy port of scatter_kv + paged_attention_varlen_materialised (reference not "
+                "installed)")
+        return (f"{what}; one sequence per step, cycling over {len(self.picks)} seeded sequences "
+                f"of {self.w['name']} (ctx {', '.join(str(int(c)) for c in self.ctx)}); "
+                f"{n_steps} steps; {os.cpu_count()} host threads")
+
+
+def cpu_baseline(w, seconds: float):
+    """About `seconds` of the reference's CPU path on sampled sequences: GB/s."""
+    g = np.random.default_rng(9)
+    ref = ReferenceCPU(w, sorted(g.choice(w["B"], size=min(3, w["B"]), replace=False).tolist()))
+    n, moved, t0 = 0, 0, time.perf_counter()
+    while True:
+        s = n % len(ref.picks)
+        ref.step(s)
+        moved += ref.bytes_of(s)
+        n += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    el = time.perf_counter() - t0
+    return {"value": round(moved / el / 1e9, 5), "unit": "GB/s", "cores": os.cpu_count(),
+            "kind": ref.kind, "sample": ref.describe(n) + f", {el:.1f} s"}
+
 
 def run_reference(args):
-    """The reference's CPU algorithm (numpy port), all host threads, rank 0 only."""
+    """--impl reference: the reference's CPU path, rank 0 only, all host threads."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
-    from tests import cases
-    from oracle import paged_oracle as O
-    w = workload(args.workload, 1)
-    g = np.random.default_rng(3)
-    seqs = 8
-    pick = np.sort(g.choice(w["B"], size=seqs, replace=False))
-    ctx = w["ctx"][pick]
-    nblk = [(int(c) + BLOCK - 1) // BLOCK for c in ctx]
-    NBs = sum(nblk)
-    tabs, at = [], 0
-    for n in nblk:
-        tabs.append(np.arange(at, at + n))
-        at += n
-    D, Hkv, Hq = w["D"], w["Hkv"], w["Hq"]
-    kp = cases.bf16_round(cases.normal(g, (1, NBs, BLOCK, Hkv, D)))
-    vp = cases.bf16_round(cases.normal(g, (1, NBs, BLOCK, Hkv, D)))
-    q = cases.bf16_round(cases.normal(g, (Hq, seqs, D)))
-    new_k = cases.bf16_round(cases.normal(g, (1, Hkv, seqs, D)))
-    flat = np.array([tabs[s][(int(ctx[s]) - 1) // BLOCK] * BLOCK + (int(ctx[s]) - 1) % BLOCK
-                     for s in range(seqs)])
-    attn_b, write_b = algorithmic_bytes(w, Hkv, Hq, batch=pick)
-    times = []
+    w = decode_workload(args.workload if args.workload in ("cfg2", "cfg5") else "cfg5")
+    g = np.random.default_rng(11)
+    picks = sorted(g.choice(w["B"], size=min(6, w["B"]), replace=False).tolist())
+    ref = ReferenceCPU(w, picks)
+    times, moved = [], 0
     for i in range(args.warmup + args.steps):
+        s = i % len(picks)
         t0 = time.perf_counter()
-        O.scatter_kv(kp, vp, 0, flat, new_k, new_k, "f32", "f32")
-        O.varlen_attention(q, kp, vp, 0, tabs, list(range(seqs)), [int(c) - 1 for c in ctx],
-                           BLOCK, scale=1.0 / math.sqrt(D))
+        ref.step(s)
+        el = time.perf_counter() - t0
         if i >= args.warmup:
-            times.append(time.perf_counter() - t0)
-    ms = statistics.mean(times) * 1e3
-    value = (attn_b + write_b) / (ms * 1e-3) / 1e9
-    sample = (f"{seqs} of {w['B']} sequences per step (sum ctx {int(ctx.sum())}); numpy port of "
-              f"scatter_kv + paged_attention_varlen_materialised, fp32 on bf16-rounded values")
-    res = {"impl": "reference", "metric": "paged-attn decode HBM GB/s (KV write + decode, algorithmic bytes)",
-           "value": round(value, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            times.append(el)
+            moved += ref.bytes_of(s)
+    total = sum(times)
+    value = moved / total / 1e9
+    ms = total / len(times) * 1e3
+    res = {"impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "GB/s",
+           "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+           "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
            "data": "synthetic (seeded)",
-           "config": {"workload": f"BASELINE {w['name']}: KV write + decode, Llama-3-8B attention",
-                      "batch": seqs},
-           "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": os.cpu_count(),
-                            "kind": "port", "sample": sample},
-           "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+           "config": {"workload": f"BASELINE {w['name']}: KV write + decode, "
+                                  f"{MODEL_OF[w['name']]} attention (Hq {w['Hq']}, Hkv {w['Hkv']}, "
+                                  f"D {w['D']}), block 16",
+                      "batch_per_step": 1, "sample": "one sequence per step (see cpu_baseline)"},
+           "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": os.cpu_count(),
+                            "kind": ref.kind, "sample": ref.describe(args.steps)},
+           "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(res), flush=True)
     return res
@@ -561,119 +709,205 @@ def run_reference(args):
 
 # ------------------------------------------------- other BASELINE configs
 
-def _pool(NB, hkv, D, dev, seed):
+def _pool(NB, hkv, D, dev, seed, layers=None):
     import torch
     g = torch.Generator(device=dev).manual_seed(seed)
-    kp = torch.randn((NB, BLOCK, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    vp = torch.randn((NB, BLOCK, hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+    shape = (NB, BLOCK, hkv, D) if layers is None else (layers, NB, BLOCK, hkv, D)
+    kp = torch.randn(shape, generator=g, device=dev, dtype=torch.bfloat16)
+    vp = torch.randn(shape, generator=g, device=dev, dtype=torch.bfloat16)
     return kp, vp, g
 
 
-def _time(fn, steps, warmup, dev):
+def _time_each(fn, steps, warmup, dev):
+    """Mean CUDA-event time of fn over `steps` launches after `warmup` (ms)."""
     import torch
     for _ in range(max(3, warmup)):
         fn()
     torch.cuda.synchronize(dev)
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
+    stream = torch.cuda.current_stream(dev)
+    pairs = []
     for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
         fn()
-    e.record()
+        b.record(stream)
+        pairs.append((a, b))
     torch.cuda.synchronize(dev)
-    return s.elapsed_time(e) / steps
+    return statistics.mean(events_ms(pairs))
 
 
-def run_cfg3(args):
+def extra_cfg2(args, dev):
+    """Config 2 (Llama-3-8B, 64 sequences): the decode step, its roofline."""
+    import torch
+    w = decode_workload("cfg2")
+    st, r = bench_decode_step(args, w, 1, 0, dev.index, dev, with_clocks=False)
+    # the same step as ONE graph (the decode a programmatic dependent launch of the write)
+    g_one, _ = capture_graph(lambda: (st.write(), st.attend()), dev)
+    one_ms = _time_each(g_one.replay, args.steps, args.warmup, dev)
+    attn_b, write_b = decode_bytes(w["ctx"], 8, 32, 128)
+    del g_one, st
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE cfg2: KV write + decode, Llama-3-8B (Hq 32, Hkv 8, D 128), "
+                        "64 sequences, ctx ~U[256,4096], 16384-block pool",
+            "value": round(r["value"], 2), "unit": "GB/s", "ms_per_step": round(r["ms_per_step"], 5),
+            "one_graph_ms_per_step": round(one_ms, 5),
+            "one_graph_value": round((attn_b + write_b) / (one_ms * 1e-3) / 1e9, 2),
+            "roofline": r["roofline"], "validated": r["validated"],
+            "attn_tokens_per_s": round(64 / (r["ms_per_step"] * 1e-3), 1)}
+
+
+def extra_cfg2_layers(args, dev, layers=32):
     """
-    One pass of BASELINE config 3: 16 prefill chunks (<= 512 tokens over a paged
-    prefix) + 48 decode tokens.  The chunk's K/V are written first (as MemForge's
-    VarlenPackedCacheLayer.update does), then one paged attention call serves
+    A 32-layer config 2 decode step: every layer's KV write + decode (each layer
+    its own 1.07 GB pool slice of one (L, blocks, 16, Hkv, D) tensor) captured as
+    one CUDA graph, each decode a programmatic dependent launch of its write.
+    Shows the per-layer rate of a whole forward's attention run back to back.
+    """
+    import torch
+    w = decode_workload("cfg2")
+    st = DecodeStep(w, 1, 0, dev, layers=layers)
+
+    def forward():
+        for l in range(layers):
+            st.write(l)
+            st.attend(None, l)
+    g, n = capture_graph(forward, dev)
+    ms = _time_each(g.replay, max(3, args.steps // 4), args.warmup, dev)
+    attn_b, write_b = decode_bytes(w["ctx"], 8, 32, 128)
+    st.K.check_device_errors(dev)
+    del g, st
+    torch.cuda.empty_cache()
+    return {"layers": layers, "ms_per_step": round(ms, 4), "per_layer_ms": round(ms / layers, 5),
+            "value": round((attn_b + write_b) * layers / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "launches_per_step": n,
+            "launch": "all layers' KV writes and decodes captured as one CUDA graph"}
+
+
+def extra_cfg3(args, dev):
+    """
+    BASELINE config 3, every chunk pass: 16 prefill chunks (<= 512 tokens over a
+    paged prefix) + 48 decode tokens per pass, passes 0.. until the prompts are
+    done.  Each pass writes the chunk's K/V, then one paged attention call serves
     every row.  Prefill FLOPs count causally visible pairs only:
-    4 * D * Hq * sum over prefill rows of (position + 1).
+    4 * D * Hq * sum over prefill rows of (position + 1).  The prefill and decode
+    sub-batches are also timed alone, for each kernel's roofline.
     """
     import torch
     from memforge_b200 import _kernels as K
     from tests import cases
-    dev = torch.device("cuda", 0)
     meta = cases.config3_meta(0)
-    q_lens, kv_lens = cases.config3_pass(meta, args.chunk_index)
-    B, Hq, Hkv, D, NB = len(q_lens), 32, 8, 128, meta["num_blocks"]
+    Hq, Hkv, D, NB = 32, 8, 128, meta["num_blocks"]
     kp, vp, g = _pool(NB, Hkv, D, dev, 3)
-    T = int(q_lens.sum())
-    q = torch.randn((T, Hq, D), generator=g, device=dev, dtype=torch.bfloat16)
-    nk = torch.randn((T, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    nv = torch.randn((T, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
-    out = torch.empty_like(q)
-    tables_np = meta["tables"].clip(min=0)
-    slots, rows_pos = [], []
-    for s_, (ql, kl) in enumerate(zip(q_lens, kv_lens)):
-        for i in range(ql):
-            pos = kl - ql + i
-            rows_pos.append(pos)
-            slots.append(int(tables_np[s_, pos // BLOCK]) * BLOCK + pos % BLOCK)
-    slots = torch.tensor(slots, dtype=torch.int32, device=dev)
-    tables = torch.from_numpy(tables_np).to(dev)
-    cu = torch.zeros(B + 1, dtype=torch.int32)
-    cu[1:] = torch.from_numpy(np.cumsum(q_lens))
-    cu = cu.to(dev)
-    kv = torch.from_numpy(kv_lens).to(dev)
     scale = 1 / math.sqrt(D)
-    maxq = int(q_lens.max())
-    # prefill-only and decode-only sub-batches, to time each kernel
-    pre = [i for i in range(B) if q_lens[i] > 1]
-    dec = [i for i in range(B) if q_lens[i] == 1]
+    tables_np = meta["tables"].clip(min=0)
+    tables = torch.from_numpy(tables_np).to(dev)
+    tot = {"flops": 0, "pre_ms": 0.0, "dbytes": 0, "dec_ms": 0.0, "ms": 0.0, "rows": 0}
+    passes = []
+    validated = None
+    for ci in range(8):
+        q_lens, kv_lens = cases.config3_pass(meta, ci)
+        pre = [i for i in range(len(q_lens)) if q_lens[i] > 1]
+        if not pre:
+            break
+        dec = [i for i in range(len(q_lens)) if q_lens[i] == 1]
+        keep = [i for i in range(len(q_lens)) if q_lens[i] > 0]
+        ql, kl = q_lens[keep], kv_lens[keep]
+        T = int(ql.sum())
+        q = torch.randn((T, Hq, D), generator=g, device=dev, dtype=torch.bfloat16)
+        nk = torch.randn((T, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+        nv = torch.randn((T, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+        out = torch.empty_like(q)
+        slots = []
+        for s_, (a, b) in zip(keep, zip(ql, kl)):
+            for i in range(int(a)):
+                p = int(b) - int(a) + i
+                slots.append(int(tables_np[s_, p // BLOCK]) * BLOCK + p % BLOCK)
+        slots = torch.tensor(slots, dtype=torch.int32, device=dev)
+        tab = tables[keep].contiguous()
+        cu = torch.zeros(len(keep) + 1, dtype=torch.int32)
+        cu[1:] = torch.from_numpy(np.cumsum(ql))
+        cu = cu.to(dev)
+        kv = torch.from_numpy(kl.astype(np.int32)).to(dev)
+        maxq = int(ql.max())
 
-    def sub(idx):
-        qi = torch.cat([q[int(cu[i]):int(cu[i + 1])] for i in idx])
-        cui = torch.zeros(len(idx) + 1, dtype=torch.int32)
-        cui[1:] = torch.from_numpy(np.cumsum(q_lens[idx]))
-        return (qi, torch.empty_like(qi), tables[idx].contiguous(), kv[idx].contiguous(),
-                cui.to(dev), int(q_lens[idx].max()))
-    P_, D_ = sub(pre), sub(dec)
+        def sub(idx):
+            sel = [keep.index(i) for i in idx]
+            rows = torch.cat([q[int(cu[j]):int(cu[j + 1])] for j in sel])
+            c = torch.zeros(len(sel) + 1, dtype=torch.int32)
+            c[1:] = torch.from_numpy(np.cumsum(ql[sel]))
+            return (rows, torch.empty_like(rows), tab[sel].contiguous(), kv[sel].contiguous(),
+                    c.to(dev), int(ql[sel].max()))
+        P_, D_ = sub(pre), sub(dec)
 
-    def full_step():
-        K.reshape_and_cache(nk, nv, kp, vp, slots)
-        K.paged_attention(q, out, kp, vp, tables, kv, cu_seqlens_q=cu, max_q_len=maxq,
-                          scale=scale)
+        def full():
+            K.reshape_and_cache(nk, nv, kp, vp, slots)
+            K.paged_attention(q, out, kp, vp, tab, kv, cu_seqlens_q=cu, max_q_len=maxq,
+                              scale=scale)
 
-    def prefill_only():
-        K.paged_attention(P_[0], P_[1], kp, vp, P_[2], P_[3], cu_seqlens_q=P_[4], max_q_len=P_[5],
-                          scale=scale)
+        def prefill_only():
+            K.paged_attention(P_[0], P_[1], kp, vp, P_[2], P_[3], cu_seqlens_q=P_[4],
+                              max_q_len=P_[5], scale=scale)
 
-    def decode_only():
-        K.paged_attention(D_[0], D_[1], kp, vp, D_[2], D_[3], cu_seqlens_q=D_[4], max_q_len=D_[5],
-                          scale=scale)
-    ms = _time(full_step, args.steps, args.warmup, dev)
-    ms_p = _time(prefill_only, args.steps, args.warmup, dev)
-    ms_d = _time(decode_only, args.steps, args.warmup, dev)
+        def decode_only():
+            K.paged_attention(D_[0], D_[1], kp, vp, D_[2], D_[3], cu_seqlens_q=D_[4],
+                              max_q_len=D_[5], scale=scale)
+        full()
+        torch.cuda.synchronize(dev)
+        if ci == 0:
+            # self-check: two prefill chunks and two decode rows against fp32 torch
+            from tests.gpu_util import torch_reference
+            worst, ok = 0.0, True
+            for j in [0, 1, len(pre), len(pre) + 1]:
+                r0, r1 = int(cu[j]), int(cu[j + 1])
+                want = torch_reference(q[r0:r1], kp, vp, tab[j:j + 1], kl[j:j + 1], ql[j:j + 1],
+                                       scale)
+                good, err = close_enough(out[r0:r1], want)
+                ok, worst = ok and good, max(worst, err)
+            if not ok:
+                raise SystemExit(f"bench self-check failed on cfg3: max |err| {worst:.3e}")
+            validated = {"chunks": 2, "decode_rows": 2, "max_abs_err": round(worst, 5), "ok": True}
+        ms = _time_each(full, args.steps, args.warmup, dev)
+        ms_p = _time_each(prefill_only, args.steps, args.warmup, dev)
+        ms_d = _time_each(decode_only, args.steps, args.warmup, dev)
+        flops = sum(4 * D * Hq * sum(int(kv_lens[i]) - int(q_lens[i]) + r + 1
+                                     for r in range(int(q_lens[i]))) for i in pre)
+        dbytes = sum(decode_bytes(kv_lens[i:i + 1], Hkv, Hq, D)[0] for i in dec)
+        passes.append({"pass": ci, "prefill_rows": int(q_lens[pre].sum()),
+                       "prefill_ms": round(ms_p, 4),
+                       "prefill_tflops": round(flops / (ms_p * 1e-3) / 1e12, 1),
+                       "decode_ms": round(ms_d, 4), "step_ms": round(ms, 4)})
+        tot["flops"] += flops
+        tot["pre_ms"] += ms_p
+        tot["dbytes"] += dbytes
+        tot["dec_ms"] += ms_d
+        tot["ms"] += ms
+        tot["rows"] += T
     K.check_device_errors(dev)
-    flops = 0
-    for i in pre:
-        ql, kl = int(q_lens[i]), int(kv_lens[i])
-        flops += 4 * D * Hq * sum(kl - ql + r + 1 for r in range(ql))
-    dbytes = sum(int(kv_lens[i]) * 2 * Hkv * D * 2 + 2 * Hq * D * 2 + ((int(kv_lens[i]) + 15) // 16) * 4
-                 for i in dec)
-    res = {"metric": "varlen chunked prefill + decode (BASELINE config 3, one pass)",
-           "workload": f"config3 pass {args.chunk_index}", "rows": T, "prefill_rows": int(q_lens[pre].sum()),
-           "ms_per_step": round(ms, 4), "attn_tokens_per_s": round(T / (ms * 1e-3), 1),
-           "prefill": {"ms": round(ms_p, 4), "tflops": round(flops / (ms_p * 1e-3) / 1e12, 2),
-                       "flops": flops},
-           "decode": {"ms": round(ms_d, 4), "GBs": round(dbytes / (ms_d * 1e-3) / 1e9, 1)},
-           "dtype": "bf16", "data": "synthetic (seeded)"}
-    print(json.dumps(res), flush=True)
+    del kp, vp
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE cfg3: varlen chunked prefill (16 prompts ~U[128,2048] in "
+                        "512-token chunks over a paged prefix ~U[0,1024]) + 48 decodes "
+                        "ctx ~U[256,4096], Llama-3-8B (Hq 32, Hkv 8, D 128); every chunk pass",
+            "passes": passes, "ms_all_passes": round(tot["ms"], 4),
+            "attn_tokens_per_s": round(tot["rows"] / (tot["ms"] * 1e-3), 1),
+            "prefill": roofline("tensor", "pf::prefill_kernel (prefill sub-batch alone)",
+                                tot["flops"], tot["pre_ms"], flops=tot["flops"],
+                                flop_rule="4*D*Hq per causally visible (query, key) pair"),
+            "decode": roofline("hbm", "tc::decode_kernel (decode sub-batch alone)",
+                               tot["dbytes"], tot["dec_ms"]),
+            "validated": validated}
 
 
-def run_cfg4(args):
+def extra_cfg4(args, dev):
     """
-    speculative verify of a 5-token window per sequence
-    (4 drafts + bonus) against the paged context, the window's K/V read from a
-    side buffer, then the commit of the accepted prefix (accepted ~U[0,4]).
+    speculative verify of a 5-token window per sequence (4
+    drafts + bonus) against the paged context, the window's K/V read from a side
+    buffer, then the commit of the accepted prefix (accepted ~U[0,4]).
     """
     import torch
     from memforge_b200 import _kernels as K
     from memforge_b200.speculative import commit_accepted, verify_attention
     from tests import cases
-    dev = torch.device("cuda", 0)
     meta = cases.config4_meta(0)
     B, Hq, Hkv, D, W, NB = 32, 40, 8, 128, meta["window"], meta["num_blocks"]
     kp, vp, g = _pool(NB, Hkv, D, dev, 4)
@@ -691,46 +925,184 @@ def run_cfg4(args):
 
     def commit():
         commit_accepted(kp, vp, wk, wv, tables, ctx, acc)
-
-    def step():
-        verify()
-        commit()
-    ms = _time(step, args.steps, args.warmup, dev)
-    ms_v = _time(verify, args.steps, args.warmup, dev)
-    ms_c = _time(commit, args.steps, args.warmup, dev)
+    verify()
+    torch.cuda.synchronize(dev)
+    from tests.gpu_util import torch_reference
+    worst, ok = 0.0, True
+    for s in (0, 7, 31):
+        want = torch_reference(q[s * W:(s + 1) * W], kp, vp, tables[s:s + 1],
+                               meta["ctx"][s:s + 1] + W, [W], 1 / math.sqrt(D),
+                               win_k=wk[s * W:(s + 1) * W], win_v=wv[s * W:(s + 1) * W])
+        good, err = close_enough(out[s * W:(s + 1) * W], want)
+        ok, worst = ok and good, max(worst, err)
+    if not ok:
+        raise SystemExit(f"bench self-check failed on cfg4: max |err| {worst:.3e}")
+    ms = _time_each(lambda: (verify(), commit()), args.steps, args.warmup, dev)
+    ms_v = _time_each(verify, args.steps, args.warmup, dev)
+    ms_c = _time_each(commit, args.steps, args.warmup, dev)
     K.check_device_errors(dev)
     ctxn = meta["ctx"].astype(np.int64)
     vbytes = int(ctxn.sum()) * 2 * Hkv * D * 2 + B * W * (Hq * D * 2 * 2 + Hkv * D * 2 * 2) + \
         int(((ctxn + 15) // 16).sum()) * 4
-    peak, kind = measured_peaks()
-    res = {"metric": "speculative verify attention HBM GB/s (BASELINE config 4)",
-           "ms_per_step": round(ms, 4), "verify_ms": round(ms_v, 4),
-           "commit_ms": round(ms_c, 4), "committed_rows": int((meta["accepted"] + 1).sum()),
-           "verify_GBs": round(vbytes / (ms_v * 1e-3) / 1e9, 1),
-           "verify_frac_of_measured_peak": round(vbytes / (ms_v * 1e-3) / 1e9 / peak, 4),
-           "attn_tokens_per_s": round(B * W / (ms * 1e-3), 1), "dtype": "bf16"}
-    print(json.dumps(res), flush=True)
+    del kp, vp
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE cfg4: speculative verify (5-token window, side buffer) + "
+                        "commit of accepted+1 rows, Qwen2.5-14B (Hq 40, Hkv 8, D 128), 32 "
+                        "sequences ctx ~U[512,8192]",
+            "ms_per_step": round(ms, 4), "verify_ms": round(ms_v, 4), "commit_ms": round(ms_c, 4),
+            "committed_rows": int((meta["accepted"] + 1).sum()),
+            "value": round(vbytes / (ms_v * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "roofline": roofline("hbm", "verify (pf::prefill_kernel, side-window tile)", vbytes,
+                                 ms_v),
+            "attn_tokens_per_s": round(B * W / (ms * 1e-3), 1),
+            "validated": {"sequences": [0, 7, 31], "max_abs_err": round(worst, 5), "ok": True}}
+
+
+TRITON_CHILD = r"""
+import json, math, os, statistics, sys
+import numpy as np, torch
+sys.path.insert(0, sys.argv[1]); sys.path.insert(0, sys.argv[2])
+from memforge_ml.kernels import triton_paged_decode as T
+from tests import cases
+meta = cases.config2_meta(0)
+dev = torch.device("cuda", 0)
+NB, B, Hq, Hkv, D = meta["num_blocks"], 64, 32, 8, 128
+g = torch.Generator(device=dev).manual_seed(1000)
+kp = torch.randn((NB * 16, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+vp = torch.randn((NB * 16, Hkv, D), generator=g, device=dev, dtype=torch.bfloat16)
+q = torch.randn((B, Hq, D), generator=g, device=dev, dtype=torch.bfloat16)
+tab = torch.from_numpy(meta["tables"].clip(min=0).astype(np.int64)).to(dev)
+ctx = torch.from_numpy(meta["ctx"].astype(np.int32)).to(dev)
+out = torch.empty_like(q)
+mx = int(meta["ctx"].max())
+f = lambda: T.paged_decode_attention(q, kp, vp, tab, ctx, 16, mx, 1 / math.sqrt(D), out=out)
+for _ in range(5):
+    f()
+torch.cuda.synchronize()
+ms = []
+for _ in range(int(sys.argv[3])):
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(); f(); b.record(); ms.append((a, b))
+torch.cuda.synchronize()
+t = statistics.mean(a.elapsed_time(b) for a, b in ms)
+print("RESULT " + json.dumps({"ms": t, "out_sum": float(out.float().abs().sum())}))
+"""
+
+
+def reference_gpu_kernel(args):
+    """The reference's Triton paged_decode_attention on this GPU at config 2 (own process)."""
+    if _reference_modules() is None:
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    try:
+        proc = subprocess.run([sys.executable, "-c", TRITON_CHILD, REF_DIR, ROOT,
+                               str(args.steps)], capture_output=True, text=True, timeout=600)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"Triton run failed: {e}"}
+    line = [x for x in proc.stdout.splitlines() if x.startswith("RESULT ")]
+    if proc.returncode != 0 or not line:
+        tail = (proc.stderr or proc.stdout).strip().splitlines()[-1:] or ["no output"]
+        return {"unavailable": f"Triton run exited {proc.returncode}: {tail[0][:200]}"}
+    d = json.loads(line[0][7:])
+    w = decode_workload("cfg2")
+    attn_b, _ = decode_bytes(w["ctx"], 8, 32, 128)
+    return {"kernel": "reference memforge_ml.kernels.triton_paged_decode.paged_decode_attention "
+                      "(num_splits 8, tile 64; its two stages)",
+            "workload": "BASELINE cfg2 decode (same lengths, tables and pool size)",
+            "ms": round(d["ms"], 5), "value": round(attn_b / (d["ms"] * 1e-3) / 1e9, 2),
+            "unit": "GB/s"}
+
+
+# ------------------------------------------------------------------- main
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from memforge_b200.build import build
+    if rank == 0 and not os.path.exists(os.path.join(ROOT, "memforge_b200", "libmemforge_sm100.so")):
+        build()
+    if world > 1:
+        dist.barrier()
+
+    w = decode_workload(args.workload)
+    st, r = bench_decode_step(args, w, world, rank, local, dev, with_clocks=(rank == 0))
+    e2e = run_e2e(args, st, world, rank, dev)
+    st.close()
+    del st
+    torch.cuda.empty_cache()
+    ms_step = r["ms_per_step"]
+    res = None
+    if rank == 0:
+        res = {
+            "metric": METRIC, "value": round(r["value"], 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded; random-init pool)",
+            "config": {"workload": f"BASELINE {w['name']}: KV write + decode, "
+                                   f"{MODEL_OF[w['name']]} attention (Hq {w['Hq']}, "
+                                   f"Hkv {w['Hkv']}, D {w['D']}), block 16",
+                       "batch": w["B"], "kv_heads_per_gpu": w["Hkv"] // world,
+                       "sum_ctx": int(w["ctx"].sum()), "pool_blocks": w["NB"],
+                       "parallelism": f"kv-head shard x{world} (strong: same sequences)"
+                       if world > 1 else "1 GPU",
+                       "l2": "inputs exceed L2 (KV read per step > 126 MB); no flush",
+                       "launch": "per step: the KV-write graph, then the decode graph"
+                                 + (", then the peer barrier" if world > 1 else "")
+                                 + "; CUDA events on the launching stream around each"},
+            "attn_tokens_per_s": round(w["B"] / (ms_step * 1e-3), 1),
+            "roofline": r["roofline"], "e2e": e2e, "gpu_launches": r["launches"],
+            "clocks": r["clocks"], "soak": r["soak"], "validated": r["validated"],
+        }
+    if world == 1 and not args.no_extras:
+        res["configs"] = {"cfg2": extra_cfg2(args, dev), "cfg3": extra_cfg3(args, dev),
+                          "cfg4": extra_cfg4(args, dev)}
+        res["cfg2_32_layers"] = extra_cfg2_layers(args, dev)
+        res["reference_gpu_kernel"] = reference_gpu_kernel(args)
+    if world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(w, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return res
+
+
+def run_single(args):
+    """--workload cfg3 / cfg4 alone (one GPU): print that config's block."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    fn = {"cfg3": extra_cfg3, "cfg4": extra_cfg4}[args.workload]
+    print(json.dumps(fn(args, dev)), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["cfg2", "cfg3", "cfg4", "cfg5"], default="cfg2")
-    ap.add_argument("--chunk-index", type=int, default=0)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", choices=["cfg5", "cfg2", "cfg3", "cfg4"], default="cfg5")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--soak-seconds", type=float, default=1.5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
-    elif args.workload == "cfg3":
-        run_cfg3(args)
-    elif args.workload == "cfg4":
-        run_cfg4(args)
+    elif args.workload in ("cfg3", "cfg4"):
+        run_single(args)
     else:
         run_ours(args)
 

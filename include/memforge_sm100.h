@@ -58,7 +58,7 @@ enum {
 #define MF_ERR_BLOCK_ID 0x1  /* block table entry outside [0, num_blocks) */
 #define MF_ERR_SLOT 0x2      /* slot_mapping entry outside [-1, num_blocks*block_size) */
 #define MF_ERR_TABLE 0x4     /* a context needs more blocks than the table row holds */
-#define MF_ERR_LENGTH 0x8    /* kv_len < q_len, or a confirmed count outside [0, window] */
+#define MF_ERR_LENGTH 0x8    /* kv_len < q_len, or a confirmed count above the window */
 #define MF_ERR_TIMEOUT 0x10  /* a bounded pipeline wait gave up */
 
 MF_API int mf_abi_version(void);
@@ -90,6 +90,25 @@ MF_API int mf_reshape_and_cache(const void* key, const void* value, mf_dtype src
                          const void* slot_mapping, int32_t slot_mapping_is_int64,
                          int32_t num_tokens, int32_t num_kv_heads, int32_t head_dim,
                          int32_t* err_flag, mf_stream_t stream);
+
+/*
+ * gather_kv — materialise a contiguous copy of some pool slots.
+ *
+ * Replaces paged_gather.gather_kv (memforge_ml/kernels/paged_gather.py:58-89)
+ * and PagedKVPool.gather / gather_flat (memforge_ml/runtime/kv_pool.py:151-179):
+ * for token t, head h, element (h, t, d) of key_out/value_out (at
+ * out + h*out_stride_head + t*out_stride_tok + d) is pool slot flat_index[t]'s
+ * element (h, d), i.e. the (1, heads, tokens, head_dim) layout the reference
+ * returns.  An index outside [0, num_blocks*block_size) sets MF_ERR_SLOT and
+ * yields zeros (the reference's index_select raises).  Bit-exact copy.
+ */
+MF_API int mf_gather_kv(const void* key_pool, const void* value_pool, mf_dtype dtype,
+                        int64_t pool_stride_block, int64_t pool_stride_slot,
+                        int64_t pool_stride_head, int32_t num_blocks, int32_t block_size,
+                        const void* flat_index, int32_t index_is_int64, int32_t num_tokens,
+                        int32_t num_kv_heads, int32_t head_dim, void* key_out,
+                        void* value_out, int64_t out_stride_head, int64_t out_stride_tok,
+                        int32_t* err_flag, mf_stream_t stream);
 
 /*
  * Paged attention over block tables: decode, speculative verify and varlen
@@ -260,9 +279,12 @@ MF_API int mf_paged_decode_noalloc(const void* q, int64_t q_stride_b, int64_t q_
  * block_size + pos%block_size of layer l (pool_stride_layer apart), for
  * j < num_confirmed[b] (the last confirmed token plus the accepted drafts).
  * Rows j >= num_confirmed[b] are not written, so the rejected slots keep their
- * contents, as in the reference.  num_confirmed outside [0, window] sets
- * MF_ERR_LENGTH, a position past the table row MF_ERR_TABLE, a block id
- * outside the pool MF_ERR_BLOCK_ID (the row is skipped in every layer).
+ * contents, as in the reference.  num_confirmed[b] <= 0 is a no-op (the
+ * reference returns early).  Each sequence's confirmed prefix is validated
+ * before any of it is written: num_confirmed above `window` sets
+ * MF_ERR_LENGTH, a confirmed position past the table row MF_ERR_TABLE, a block
+ * id outside the pool MF_ERR_BLOCK_ID, and then none of that sequence's rows is
+ * written in any layer (where the reference raises IndexError before writing).
  * Dtype pairs and rounding as mf_reshape_and_cache.  All integer inputs live
  * on the device, so the call is CUDA-graph safe.
  */

@@ -10,8 +10,9 @@ Workspace and error word
 * The attention kernels keep split-K partials and arrival counters in a
   zero-initialised workspace they leave zeroed.  One is cached per device and
   grown on demand; make one warm-up call before capturing a CUDA graph so the
-  capture does not allocate.  Launches on different streams that may overlap
-  must pass their own ``workspace=``.
+  capture does not allocate.  A workspace that is outgrown stays allocated, so
+  graphs captured on it keep a valid address.  Launches on different streams
+  that may overlap must pass their own ``workspace=``.
 * Kernels report bad block ids, slots past the pool, too-short block tables and
   expired waits by OR-ing bits into a per-device int32 error word.  With
   ``MEMFORGE_CHECK=1`` (or ``set_checks(True)``) every call synchronises and
@@ -32,10 +33,11 @@ DTYPES = {torch.float32: L.MF_F32, torch.float16: L.MF_F16, torch.bfloat16: L.MF
 
 _state_lock = threading.Lock()
 _workspaces: Dict[int, torch.Tensor] = {}
+_retired: list = []   # grown-out workspaces, kept alive for graphs that captured them
 _err_words: Dict[int, torch.Tensor] = {}
 _checks = os.environ.get("MEMFORGE_CHECK", "0") not in ("", "0")
 launch_counter = {"reshape_and_cache": 0, "paged_attention": 0, "copy_blocks": 0,
-                  "peer_barrier": 0, "commit_window": 0}
+                  "peer_barrier": 0, "commit_window": 0, "gather_kv": 0}
 
 
 def set_checks(enabled: bool) -> None:
@@ -99,6 +101,8 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
             ws = _workspaces.get(idx)
             if ws is None or ws.numel() < nbytes:
                 size = max(nbytes, 1 << 20)
+                if ws is not None:
+                    _retired.append(ws)
                 ws = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
                 _workspaces[idx] = ws
     return ws
@@ -167,6 +171,44 @@ def reshape_and_cache(key: torch.Tensor, value: torch.Tensor, key_pool: torch.Te
     L.check(rc, "mf_reshape_and_cache")
     launch_counter["reshape_and_cache"] += 1
     _after("reshape_and_cache", dev)
+
+
+def gather_kv(key_pool: torch.Tensor, value_pool: torch.Tensor, flat_index: torch.Tensor,
+              heads_major: bool = False):
+    """
+    ``mf_gather_kv``: the pool slots ``flat_index`` (int32/int64 CUDA tensor) of
+    one layer ``(blocks, block_size, H, D)`` (or ``(blocks, H, block_size, D)``
+    with ``heads_major``) as contiguous ``(1, H, T, D)`` keys and values.
+    """
+    require_cuda("gather_kv", key_pool, value_pool)
+    if flat_index.device != key_pool.device:
+        flat_index = flat_index.to(key_pool.device)
+    if key_pool.stride(-1) != 1 or value_pool.stride() != key_pool.stride():
+        raise ValueError("pool layers must share strides and have a contiguous last dim")
+    if flat_index.dtype not in (torch.int32, torch.int64):
+        raise TypeError("flat_index must be int32 or int64")
+    flat_index = flat_index.reshape(-1).contiguous()
+    if heads_major:
+        nb, H, bs, D = key_pool.shape
+        sb, sh, ss = key_pool.stride(0), key_pool.stride(1), key_pool.stride(2)
+    else:
+        nb, bs, H, D = key_pool.shape
+        sb, ss, sh = key_pool.stride(0), key_pool.stride(1), key_pool.stride(2)
+    T = flat_index.numel()
+    k = torch.empty((1, H, T, D), dtype=key_pool.dtype, device=key_pool.device)
+    v = torch.empty_like(k)
+    if T == 0:
+        return k, v
+    dev = key_pool.device
+    rc = L.lib().mf_gather_kv(key_pool.data_ptr(), value_pool.data_ptr(),
+                              dtype_code(key_pool.dtype), sb, ss, sh, nb, bs,
+                              flat_index.data_ptr(), 1 if flat_index.dtype == torch.int64 else 0,
+                              T, H, D, k.data_ptr(), v.data_ptr(), T * D, D,
+                              err_word(dev).data_ptr(), _stream_ptr(dev))
+    L.check(rc, "mf_gather_kv")
+    launch_counter["gather_kv"] += 1
+    _after("gather_kv", dev)
+    return k, v
 
 
 def commit_window(win_k: torch.Tensor, win_v: torch.Tensor, key_pool: torch.Tensor,

@@ -35,8 +35,8 @@ ERR_NAMES = {
     MF_ERR_BLOCK_ID: "block table entry outside the pool",
     MF_ERR_SLOT: "slot_mapping entry outside the pool",
     MF_ERR_TABLE: "context needs more blocks than the block table holds",
-    MF_ERR_LENGTH: "length out of range (kv_len < q_len, or a confirmed count outside "
-                   "[0, window])",
+    MF_ERR_LENGTH: "length out of range (kv_len < q_len, or a confirmed count above the "
+                   "window)",
     MF_ERR_TIMEOUT: "a bounded pipeline wait gave up",
 }
 
@@ -45,7 +45,7 @@ EXPORTED = (
     "mf_abi_version", "mf_last_error", "mf_device_info", "mf_reshape_and_cache",
     "mf_paged_attention_workspace_size", "mf_paged_attention", "mf_paged_decode",
     "mf_copy_blocks", "mf_paged_decode_noalloc", "mf_peer_barrier", "mf_ipc_export",
-    "mf_ipc_open", "mf_ipc_close", "mf_commit_window",
+    "mf_ipc_open", "mf_ipc_close", "mf_commit_window", "mf_gather_kv",
 )
 
 MF_IPC_HANDLE_BYTES = 64
@@ -103,6 +103,9 @@ def _declare(lib):
     lib.mf_paged_decode.argtypes = [
         c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i32, c_vp, c_i32, c_vp, c_i32,
         c_i32, c_i32, c_i32, c_i32, c_f32, ctypes.c_int, c_vp, c_vp, c_sz, c_vp, c_vp]
+    lib.mf_gather_kv.argtypes = [
+        c_vp, c_vp, ctypes.c_int, c_i64, c_i64, c_i64, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32,
+        c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]
     lib.mf_copy_blocks.argtypes = [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp, c_vp]
     lib.mf_commit_window.argtypes = [
         c_vp, c_vp, ctypes.c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,

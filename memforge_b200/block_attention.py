@@ -47,17 +47,3 @@ def paged_attention_blockwise(query: torch.Tensor, key_pool: torch.Tensor,
     K.paged_attention(q[0].permute(1, 0, 2), out[0].permute(1, 0, 2), key_pool[layer_idx],
                       value_pool[layer_idx], table, kv, q_per_seq=1, scale=scale, causal=True)
     return out
-
-
-def reference_attention(query: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
-                        scale: Optional[float] = None) -> torch.Tensor:
-    """Plain single-query attention over a materialised context (``block_attention.py:148-174``)."""
-    num_heads, head_dim = query.shape[1], query.shape[3]
-    group = num_heads // keys.shape[1]
-    scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
-    k, v = keys.float(), values.float()
-    if group > 1:
-        k = k.repeat_interleave(group, dim=1)
-        v = v.repeat_interleave(group, dim=1)
-    w = torch.softmax(torch.einsum("bhqd,bhtd->bhqt", query.float(), k) * scale, dim=-1)
-    return torch.einsum("bhqt,bhtd->bhqd", w, v).to(query.dtype)

@@ -1,6 +1,6 @@
 // KV writes into the paged pool: reshape_and_cache (slot-mapping scatter), the
 // speculative commit of a window's confirmed rows, and the all-layer
-// copy-on-write block copy.
+// copy-on-write block copy; and the materialising read (gather_kv).
 //
 // Both are byte-moving kernels bounded by HBM: every thread moves one 16-byte
 // vector (8 bf16 / 4 fp32 elements) when the row is 16-byte aligned, so each
@@ -71,9 +71,11 @@ MF_DEVINL void copy_row_vec(const S* __restrict__ src, P* __restrict__ dst, int 
 // ctx[b] + j, through b's block table, for j < num_confirmed[b]; the other rows
 // (rejected drafts) are not written, so their slots keep what they held.  The
 // slot arithmetic of PagedKVPool.slot_indices (memforge_ml/runtime/
-// kv_pool.py:92-130) runs on the device; a position past the table row or a
-// block id outside the pool sets an error bit and skips the row, as the
-// reference's IndexError would stop the write.
+// kv_pool.py:92-130) runs on the device.  A confirmed count of 0 or less is a
+// no-op (scatter_accepted_kv returns early); a count above the window, a
+// confirmed position past the table row or a block id outside the pool sets an
+// error bit and skips every row of that sequence in every layer, as the
+// reference's IndexError stops the write before it starts.
 template <typename S, typename P>
 __global__ void commit_window_kernel(const S* __restrict__ wk, const S* __restrict__ wv,
                                      int64_t k_stride_layer, int64_t k_stride_row,
@@ -99,25 +101,36 @@ __global__ void commit_window_kernel(const S* __restrict__ wk, const S* __restri
     const int h = (int)(rh % num_heads);
     const int64_t r = rh / num_heads;  // window row, sequence-major
     const int b = (int)(r / window), j = (int)(r % window);
-    const bool lead = v == 0 && h == 0 && layer == 0;  // one error report per row
+    // One error report per sequence.  The whole confirmed prefix is validated
+    // before any of its rows is written, so a sequence the reference would
+    // reject (IndexError from slot_indices before the first layer's write)
+    // leaves the pool untouched in every layer.
+    const bool lead = v == 0 && h == 0 && layer == 0 && j == 0;
     const int n = __ldg(num_confirmed + b);
     const int c = __ldg(ctx_lens + b);
-    if (n < 0 || n > window || c < 0) {
-      if (lead && j == 0) set_err(err, MF_ERR_LENGTH);
+    if (n <= 0 || j >= n) continue;  // nothing confirmed: a no-op, as in the reference
+    if (n > window || c < 0) {
+      if (lead) set_err(err, MF_ERR_LENGTH);
       continue;
     }
-    if (j >= n) continue;
-    const int64_t pos = (int64_t)c + j;
-    const int64_t page = pos / block_size;
-    if (page >= table_stride) {
+    const int64_t first_page = (int64_t)c / block_size;
+    const int64_t last_page = ((int64_t)c + n - 1) / block_size;
+    if (last_page >= table_stride) {
       if (lead) set_err(err, MF_ERR_TABLE);
       continue;
     }
-    const int blk = __ldg(tables + (int64_t)b * table_stride + page);
-    if (blk < 0 || blk >= num_blocks) {
+    bool ids_ok = true;
+    for (int64_t p = first_page; p <= last_page; ++p) {
+      const int id = __ldg(tables + (int64_t)b * table_stride + p);
+      ids_ok = ids_ok && id >= 0 && id < num_blocks;
+    }
+    if (!ids_ok) {
       if (lead) set_err(err, MF_ERR_BLOCK_ID);
       continue;
     }
+    const int64_t pos = (int64_t)c + j;
+    const int64_t page = pos / block_size;
+    const int blk = __ldg(tables + (int64_t)b * table_stride + page);
     const int64_t dst_off = layer * sl + (int64_t)blk * sb + (pos % block_size) * ss + h * sh +
                             (int64_t)v * vec;
     copy_row_vec<S, P>(
@@ -126,6 +139,45 @@ __global__ void commit_window_kernel(const S* __restrict__ wk, const S* __restri
     copy_row_vec<S, P>(
         wv + layer * v_stride_layer + r * v_stride_row + h * v_stride_head + (int64_t)v * vec,
         value_pool + dst_off, vec);
+  }
+}
+
+// Materialising read (paged_gather.gather_kv / PagedKVPool.gather_flat,
+// memforge_ml/kernels/paged_gather.py:58-89): output row t holds pool slot
+// flat_index[t] for every kv head, written head-major (element (h, t, d) at
+// out + h*o_sh + t*o_st + d), the (1, H, T, D) layout the reference returns.
+// One work item = (token, head, vector of `vec` elements): a warp reads one
+// slot's heads contiguously and writes each head's row as whole 16-byte
+// vectors.  A slot outside the pool sets MF_ERR_SLOT and yields zeros.
+template <typename T>
+__global__ void gather_kv_kernel(const T* __restrict__ kp, const T* __restrict__ vp, int64_t sb,
+                                 int64_t ss, int64_t sh, int64_t num_slots, int32_t block_size,
+                                 const void* __restrict__ index, int index64, int num_tokens,
+                                 int num_heads, int head_dim, int vec, T* __restrict__ ko,
+                                 T* __restrict__ vo, int64_t o_sh, int64_t o_st, int32_t* err) {
+  const int vecs_per_row = head_dim / vec;
+  const int64_t total = (int64_t)num_tokens * num_heads * vecs_per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vecs_per_row);
+    const int64_t th = i / vecs_per_row;
+    const int h = (int)(th % num_heads);
+    const int t = (int)(th / num_heads);
+    const int64_t slot = index64 ? reinterpret_cast<const int64_t*>(index)[t]
+                                 : (int64_t)reinterpret_cast<const int32_t*>(index)[t];
+    T* kd = ko + h * o_sh + (int64_t)t * o_st + (int64_t)v * vec;
+    T* vd = vo + h * o_sh + (int64_t)t * o_st + (int64_t)v * vec;
+    if (slot < 0 || slot >= num_slots) {
+      if (v == 0 && h == 0) set_err(err, MF_ERR_SLOT);
+      for (int j = 0; j < vec; ++j) {
+        kd[j] = from_f32<T>(0.f);
+        vd[j] = from_f32<T>(0.f);
+      }
+      continue;
+    }
+    const int64_t src = (slot / block_size) * sb + (slot % block_size) * ss + h * sh + (int64_t)v * vec;
+    copy_row_vec<T, T>(kp + src, kd, vec);
+    copy_row_vec<T, T>(vp + src, vd, vec);
   }
 }
 
@@ -187,6 +239,29 @@ int launch_rac(const void* key, const void* value, int64_t kst, int64_t ksh, int
       static_cast<P*>(kp), static_cast<P*>(vp), sb, ss, sh, num_slots, bs, slots, slots64, T, H,
       D, vec, err);
   return check_launch("reshape_and_cache");
+}
+
+template <typename T>
+int launch_gather(const void* kp, const void* vp, int64_t sb, int64_t ss, int64_t sh,
+                  int64_t num_slots, int32_t bs, const void* index, int index64, int T_, int H,
+                  int D, void* ko, void* vo, int64_t o_sh, int64_t o_st, int32_t* err,
+                  cudaStream_t stream) {
+  int vec = 1;
+  const int v16 = 16 / (int)sizeof(T);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  auto al16 = [](int64_t stride) { return (stride * (int64_t)sizeof(T)) % 16 == 0; };
+  if (D % v16 == 0 && al(kp) && al(vp) && al(ko) && al(vo) && al16(sb) && al16(ss) &&
+      al16(sh) && al16(o_sh) && al16(o_st)) {
+    vec = v16;
+  }
+  const int64_t items = (int64_t)T_ * H * (D / vec);
+  const int threads = 256;
+  int64_t blocks = (items + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  gather_kv_kernel<T><<<(unsigned)blocks, threads, 0, stream>>>(
+      static_cast<const T*>(kp), static_cast<const T*>(vp), sb, ss, sh, num_slots, bs, index,
+      index64, T_, H, D, vec, static_cast<T*>(ko), static_cast<T*>(vo), o_sh, o_st, err);
+  return check_launch("gather_kv");
 }
 
 template <typename S, typename P>
@@ -316,4 +391,31 @@ extern "C" int mf_commit_window(const void* win_k, const void* win_v, mf_dtype s
   }
 #undef MF_COMMIT
   return fail(MF_EUNSUPPORTED, "commit_window: unsupported (src, pool) dtype pair");
+}
+
+extern "C" int mf_gather_kv(const void* key_pool, const void* value_pool, mf_dtype dtype,
+                            int64_t pool_stride_block, int64_t pool_stride_slot,
+                            int64_t pool_stride_head, int32_t num_blocks, int32_t block_size,
+                            const void* flat_index, int32_t index_is_int64, int32_t num_tokens,
+                            int32_t num_kv_heads, int32_t head_dim, void* key_out,
+                            void* value_out, int64_t out_stride_head, int64_t out_stride_tok,
+                            int32_t* err_flag, mf_stream_t stream) {
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 ||
+      num_blocks <= 0)
+    return fail(MF_EINVAL, "gather_kv: non-positive size");
+  if (num_tokens == 0) return MF_OK;
+  if (!key_pool || !value_pool || !flat_index || !key_out || !value_out)
+    return fail(MF_EINVAL, "gather_kv: null pointer");
+  const int64_t num_slots = (int64_t)num_blocks * block_size;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+#define MF_GATHER(T)                                                                          \
+  return launch_gather<T>(key_pool, value_pool, pool_stride_block, pool_stride_slot,          \
+                          pool_stride_head, num_slots, block_size, flat_index, index_is_int64, \
+                          num_tokens, num_kv_heads, head_dim, key_out, value_out,              \
+                          out_stride_head, out_stride_tok, err_flag, s)
+  if (dtype == MF_F32) MF_GATHER(float);
+  if (dtype == MF_F16) MF_GATHER(__half);
+  if (dtype == MF_BF16) MF_GATHER(__nv_bfloat16);
+#undef MF_GATHER
+  return fail(MF_EUNSUPPORTED, "gather_kv: unsupported dtype");
 }

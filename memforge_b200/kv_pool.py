@@ -98,12 +98,12 @@ class PagedKVPool:
 
     def gather(self, layer_idx: int, physical: torch.Tensor,
                slots: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-        k = self.key_pool[layer_idx, physical, slots]
-        v = self.value_pool[layer_idx, physical, slots]
-        return (k.permute(1, 0, 2).unsqueeze(0).contiguous(),
-                v.permute(1, 0, 2).unsqueeze(0).contiguous())
+        """Contiguous ``(1, H, T, D)`` K/V at (physical, slot) (``kv_pool.py:151-170``)."""
+        flat = paged_gather.flat_slot_index(physical, slots, self.block_size)
+        return self.gather_flat(layer_idx, flat)
 
     def gather_flat(self, layer_idx: int, flat_index: torch.Tensor):
+        """``kv_pool.py:172-179``: one gather kernel for K and V."""
         return paged_gather.gather_kv(self.key_pool, self.value_pool, layer_idx, flat_index,
                                       self.block_size)
 

@@ -112,9 +112,16 @@ class PeerOutput:
     (``mf_ipc_open``, with peer access enabled).  ``pointers(b)`` are the
     addresses of buffer ``b`` on all GPUs as this process sees them, for
     ``mf_attention_args.out_peers``; ``barrier()`` runs ``mf_peer_barrier`` with
-    the next epoch.  Buffers alternate per step: the barrier of step i
-    guarantees that every rank has finished step i-1, so the stores of step i+1
-    never hit a buffer a peer may still read.  Construction and ``close`` are
+    the next epoch.  Buffers alternate per step (``buffers`` of them, 2 by
+    default).  The barrier of step i orders only each rank's own stream: once
+    it completes, every rank has launched, on its stream, everything it queued
+    before its step-i attention.  So the rule for callers is: every read of
+    ``outs[b]`` (an o_proj, a copy to the host) must be stream-ordered on this
+    rank's stream before the rank's next ``step_peer`` call.  Then the stores
+    that peers make into buffer b two steps later cannot overtake it.  A reader
+    on a side stream, or one that runs asynchronously past the next step, needs
+    that stream joined first, or more buffers (``buffers=k`` keeps a buffer
+    untouched for k-1 further steps).  Construction and ``close`` are
     collective (all ranks, same arguments).
     """
 

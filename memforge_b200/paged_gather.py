@@ -2,9 +2,10 @@
 Paged KV gather and scatter, B200 edition of ``memforge_ml/kernels/paged_gather.py``.
 
 ``scatter_kv`` (the reshape_and_cache hot op) runs the sm_100a slot-mapping
-scatter kernel; ``flat_slot_index`` is the same integer arithmetic as the
-reference; ``gather_kv`` keeps the reference's materialising read for callers
-that still want a contiguous context (the attention kernels never need it).
+scatter kernel; ``gather_kv`` the gather kernel (``mf_gather_kv``), the
+materialising read for callers that still want a contiguous context (the
+attention kernels never need it); ``flat_slot_index`` is the same integer
+arithmetic as the reference.
 """
 
 from __future__ import annotations
@@ -26,19 +27,13 @@ def gather_kv(key_pool: torch.Tensor, value_pool: torch.Tensor, layer_idx: int,
               flat_index: torch.Tensor, block_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """
     Materialise ``(1, heads, tokens, head_dim)`` K/V of one layer
-    (``paged_gather.py:58-89``).  A plain index_select: the attention kernels
-    read pages in place and never call this.
+    (``paged_gather.py:58-89``) with one gather launch for K and V.
     """
-    num_blocks, slots_per_block = key_pool.shape[1], key_pool.shape[2]
+    slots_per_block = key_pool.shape[2]
     assert slots_per_block == block_size, (
         f"pool block size {slots_per_block} does not match {block_size}"
     )
-    flat_k = key_pool[layer_idx].view(num_blocks * slots_per_block, *key_pool.shape[3:])
-    flat_v = value_pool[layer_idx].view(num_blocks * slots_per_block, *value_pool.shape[3:])
-    k = torch.index_select(flat_k, 0, flat_index)
-    v = torch.index_select(flat_v, 0, flat_index)
-    return (k.permute(1, 0, 2).unsqueeze(0).contiguous(),
-            v.permute(1, 0, 2).unsqueeze(0).contiguous())
+    return K.gather_kv(key_pool[layer_idx], value_pool[layer_idx], flat_index)
 
 
 _NARROWING = {(torch.float32, torch.bfloat16), (torch.float32, torch.float16)}

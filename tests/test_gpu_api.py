@@ -148,6 +148,47 @@ def test_each_layer_reads_its_own_slice():
     assert not torch.allclose(outs[1], outs[2], atol=1e-4)
 
 
+def test_varlen_with_device_tables_is_graph_capturable():
+    """The seam reads device tables on the device: after one warm-up call a CUDA
+    graph of it replays with new table contents, pool values and queries."""
+    from memforge_b200.varlen_attention import paged_attention_varlen
+    pool = _small_pool(block=16, head_dim=64, num_blocks=64, kv_heads=2)
+    tabs = [t.cuda() for t in _tables([70, 33, 120], block=16)]
+    sid = [0, 0, 0, 1, 2, 2]
+    pos = [66, 67, 68, 32, 100, 101]
+    q = torch.randn(1, 4, 6, 64, device="cuda")
+    paged_attention_varlen(q, pool.key_pool, pool.value_pool, 1, tabs, sid, pos, 16)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            out = paged_attention_varlen(q, pool.key_pool, pool.value_pool, 1, tabs, sid, pos, 16)
+    torch.cuda.current_stream().wait_stream(s)
+    for trial in range(3):
+        q.normal_()
+        pool.key_pool[1].normal_()
+        tabs[1].copy_(torch.randperm(64, device="cuda")[:tabs[1].numel()])
+        g.replay()
+        want = paged_attention_varlen(q, pool.key_pool, pool.value_pool, 1, tabs, sid, pos, 16)
+        torch.cuda.synchronize()
+        assert torch.allclose(out, want, atol=ATOL), trial
+
+
+def test_varlen_metadata_is_uploaded_once_per_pass():
+    """Every layer of a pass reuses the plan: no host work beyond the first layer's."""
+    from memforge_b200 import varlen_attention as V
+    pool = _small_pool(block=4)
+    tabs = [t.cuda() for t in _tables([13, 6, 20])]
+    sid, pos = [0, 0, 1, 2], [11, 12, 5, 19]
+    q = torch.randn(1, 4, 4, 8, device="cuda")
+    V._memo.clear()
+    for layer in range(2):
+        V.paged_attention_varlen(q, pool.key_pool, pool.value_pool, layer, tabs, sid, pos, 4)
+    assert len(V._memo) == 1
+
+
 def test_varlen_validation_matches_reference():
     from memforge_b200.varlen_attention import paged_attention_varlen
     pool = _small_pool()

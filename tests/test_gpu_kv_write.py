@@ -132,3 +132,59 @@ def test_copy_blocks_all_layers_bit_exact():
         ref_v[:, d] = ref_v[:, s]
     torch.cuda.synchronize()
     assert torch.equal(kp, ref_k) and torch.equal(vp, ref_v)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("idx_dtype", [torch.int32, torch.int64])
+def test_gather_kv_matches_index_select_bit_exact(dtype, idx_dtype):
+    """gather_kv / PagedKVPool.gather_flat (paged_gather.py:58-89): (1, H, T, D) copies."""
+    from memforge_b200.paged_gather import gather_kv
+    L_, NB, H, D = 3, 40, 4, 128
+    kp = torch.randn(L_, NB, 16, H, D, device="cuda").to(dtype)
+    vp = torch.randn_like(kp)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    flat = torch.randint(0, NB * 16, (333,), generator=g, device="cuda").to(idx_dtype)
+    k, v = gather_kv(kp, vp, 2, flat, 16)
+    want_k = kp[2].view(NB * 16, H, D).index_select(0, flat.long()).permute(1, 0, 2)[None]
+    want_v = vp[2].view(NB * 16, H, D).index_select(0, flat.long()).permute(1, 0, 2)[None]
+    torch.cuda.synchronize()
+    assert k.shape == (1, H, 333, D) and k.is_contiguous()
+    assert torch.equal(k, want_k) and torch.equal(v, want_v)
+
+
+def test_gather_kv_odd_head_dim_and_heads_major_layout():
+    from memforge_b200 import _kernels as K
+    NB, H, D = 12, 3, 40
+    cache = torch.randn(NB, H, 16, D, device="cuda")          # standalone operator layout
+    flat = torch.tensor([5, 0, 191, 77, 16], device="cuda")
+    k, v = K.gather_kv(cache, cache, flat, heads_major=True)
+    want = cache.permute(0, 2, 1, 3).reshape(NB * 16, H, D)[flat].permute(1, 0, 2)[None]
+    assert torch.equal(k, want) and torch.equal(v, want)
+
+
+def test_gather_kv_bad_index_reports_and_zero_fills():
+    from memforge_b200.paged_gather import gather_kv
+    kp = torch.randn(1, 4, 16, 2, 64, device="cuda").bfloat16()
+    flat = torch.tensor([3, 64, -2, 7], device="cuda")     # 64 is past 4*16
+    k, _ = gather_kv(kp, kp, 0, flat, 16)
+    with pytest.raises(IndexError, match="slot_mapping"):
+        K.check_device_errors(kp.device)
+    assert torch.equal(k[0, :, 0], kp[0].view(64, 2, 64)[3])
+    assert float(k[0, :, 1].float().abs().sum()) == 0.0
+    assert float(k[0, :, 2].float().abs().sum()) == 0.0
+
+
+def test_pool_gather_uses_the_kernel_and_matches_the_write():
+    """PagedKVPool.write then PagedKVPool.gather returns the rows written (round trip)."""
+    from memforge_b200.kv_pool import ModelKVSpec, PagedKVPool
+    spec = ModelKVSpec(num_layers=2, num_kv_heads=2, head_dim=64, dtype=torch.bfloat16,
+                       device="cuda")
+    pool = PagedKVPool(spec, num_blocks=10, block_size=16)
+    table = torch.tensor([7, 2, 9], device="cuda")
+    phys, slots = pool.slot_indices(table, 5, 40)
+    keys = torch.randn(1, 2, 35, 64, device="cuda").bfloat16()
+    before = K.launch_counter["gather_kv"]
+    pool.write(1, phys, slots, keys, keys * 2)
+    k, v = pool.gather(1, phys, slots)
+    assert K.launch_counter["gather_kv"] == before + 1
+    assert torch.equal(k, keys) and torch.equal(v, keys * 2)

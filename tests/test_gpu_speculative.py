@@ -137,13 +137,17 @@ def test_commit_window_bit_exact_with_page_crossings(src, pool):
     assert np.array_equal(_bits(vp), _want_bits(want_v, pool))
 
 
-def test_commit_window_errors_skip_rows_and_set_bits():
+def test_commit_window_errors_skip_whole_sequences_and_set_bits():
+    """A sequence the reference would reject (IndexError from slot_indices before
+    the first write) writes nothing; a confirmed count <= 0 is a silent no-op."""
     from memforge_b200 import _kernels as K
     W, width = 4, 2
-    ctx = [30, 5, 5, 5]
-    conf = [4, 5, 2, 1]   # seq 0 crosses past its 2-page table; seq 1 confirms more than W
+    ctx = [30, 5, 5, 5, 5, 5]
+    # seq 0 crosses past its 2-page table; seq 1 confirms more than W; seq 3
+    # names a block outside the pool; seqs 4 and 5 confirm nothing
+    conf = [4, 5, 2, 1, 0, -2]
     kp0, vp0, tables, wk, wv = _commit_case(41, ctx, W, width=width)
-    tables[3, 0] = 999    # block id outside the pool
+    tables[3, 0] = 999
     kp, vp = to_dev(kp0, "bf16"), to_dev(vp0, "bf16")
     dk, dv = to_dev(wk, "bf16"), to_dev(wv, "bf16")
     K.commit_window(dk, dv, kp, vp, torch.from_numpy(tables).cuda(),
@@ -153,11 +157,27 @@ def test_commit_window_errors_skip_rows_and_set_bits():
     with pytest.raises(IndexError):
         K.check_device_errors(kp.device)
     assert bits == 0x1 | 0x4 | 0x8, hex(bits)
-    # What the kernel still writes: seq 0's rows inside the table (positions 30, 31),
-    # all of seq 2's confirmed rows; nothing of seq 1 or seq 3.
-    want_k, _ = _oracle_commit(kp0, vp0, tables, [30, 5, 5, 5],
-                               wk, wv, [2, 0, 2, 0], W, "bf16", "bf16")
+    # Only seq 2's confirmed rows land; seq 0's in-table positions 30, 31 stay untouched.
+    want_k, want_v = _oracle_commit(kp0, vp0, tables, ctx, wk, wv, [0, 0, 2, 0, 0, 0], W,
+                                    "bf16", "bf16")
     assert np.array_equal(_bits(kp), _want_bits(want_k, "bf16"))
+    assert np.array_equal(_bits(vp), _want_bits(want_v, "bf16"))
+
+
+def test_commit_window_nothing_confirmed_is_silent():
+    from memforge_b200 import _kernels as K
+    W = 5
+    ctx = [7, 40]
+    kp0, vp0, tables, wk, wv = _commit_case(42, ctx, W)
+    kp, vp = to_dev(kp0, "bf16"), to_dev(vp0, "bf16")
+    before = kp.clone()
+    K.commit_window(to_dev(wk, "bf16"), to_dev(wv, "bf16"), kp, vp,
+                    torch.from_numpy(tables).cuda(),
+                    torch.tensor(ctx, dtype=torch.int32, device="cuda"),
+                    torch.tensor([0, -1], dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    assert int(K.err_word(kp.device).item()) == 0
+    assert torch.equal(kp, before)
 
 
 def test_commit_window_all_layers_in_one_launch():

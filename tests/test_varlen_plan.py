@@ -58,9 +58,36 @@ def test_reference_validation_messages():
 
 
 def test_packed_buffer_round_trip():
-    p = plan_varlen(4, tables(11, 6, 20), [1, 0, 2, 0], [5, 9, 19, 10], 4, 8, 2)
-    buf, offs = p.packed()
+    t = tables(11, 6, 20)
+    p = plan_varlen(4, t, [1, 0, 2, 0], [5, 9, 19, 10], 4, 8, 2)
+    buf, offs = p.packed(t)
+    host = p.host_tables(t)
     o, n = offs["tables"]
-    assert np.array_equal(buf[o:o + n].reshape(p.tables.shape), p.tables)
+    assert np.array_equal(buf[o:o + n].reshape(host.shape), host)
     o, n = offs["row_map"]
     assert np.array_equal(buf[o:o + n], p.row_map)
+
+
+def test_segment_tables_hold_each_sequences_needed_prefix():
+    t = tables(11, 6, 20)
+    p = plan_varlen(4, t, [1, 0, 2, 0], [5, 9, 19, 10], 4, 8, 2)
+    host = p.host_tables(t)
+    # segments: seq 1 (6 keys, 2 blocks), seq 0 (11 keys, 3 blocks), seq 2 (20 keys, 5 blocks)
+    assert p.seg_seq.tolist() == [1, 0, 2]
+    assert p.needed.tolist() == [2, 3, 5]
+    assert host.shape == (3, 5)
+    for i, (sq, n) in enumerate(zip(p.seg_seq, p.needed)):
+        assert host[i, :n].tolist() == t[sq][:n].tolist()
+        assert (host[i, n:] == 0).all()
+
+
+def test_planning_reads_table_lengths_only():
+    """Tables whose contents cannot be read on the host (only sizes) still plan."""
+    class SizedOnly:
+        def __init__(self, n):
+            self.n = n
+
+        def numel(self):
+            return self.n
+    p = plan_varlen(3, [SizedOnly(3), SizedOnly(5)], [1, 1, 0], [8, 9, 2], 4, 4, 2)
+    assert p.kv_lens.tolist() == [10, 3] and p.needed.tolist() == [3, 1]

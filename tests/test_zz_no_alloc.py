@@ -79,13 +79,21 @@ def _workspace_for(q, k, tables, ctx):
     return torch.zeros(max(need, 1), dtype=torch.uint8, device="cuda")
 
 
+# Two calls whose split-K plans differ (batch, head geometry and context
+# lengths), so the second call's ranges and arrival counters are not the
+# first call's.  Both entry points run the same kernel with the same plan and
+# the same fixed merge order, so their outputs must be bit-identical.
+CALLS = [dict(seed=11, B=24, Hq=32, Hkv=8, max_ctx=3000),
+         dict(seed=12, B=7, Hq=16, Hkv=2, max_ctx=6000)]
+
+
 def test_noalloc_decode_matches_the_workspace_entry_point_twice():
-    for call, seed in enumerate((11, 12)):
-        q, k, v, tables, ctx = _case(seed)
+    for call, kw in enumerate(CALLS):
+        q, k, v, tables, ctx = _case(kw["seed"], B=kw["B"], Hq=kw["Hq"], Hkv=kw["Hkv"],
+                                     max_ctx=kw["max_ctx"])
         ws = _workspace_for(q, k, tables, ctx)
         want = _call("mf_paged_decode", q, k, v, tables, ctx, torch.empty_like(q), ws)
         got = _call("mf_paged_decode_noalloc", q, k, v, tables, ctx, torch.empty_like(q))
-        err = (got.float() - want.float()).abs()
         assert torch.isfinite(got).all()
-        assert bool((err <= 2e-2 + 1e-2 * want.float().abs()).all()), \
-            f"call {call}: max |diff| {float(err.max()):.3e}"
+        diff = (got.float() - want.float()).abs()
+        assert torch.equal(got, want), f"call {call}: max |diff| {float(diff.max()):.3e}"
