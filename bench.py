@@ -89,17 +89,26 @@ MODEL_OF = {"cfg2": "Llama-3-8B", "cfg5": "Llama-3-70B", "cfg4": "Qwen2.5-14B",
             "cfg3": "Llama-3-8B"}
 
 
-def decode_workload(name: str):
-    """Host-side metadata of a decode-step workload (identical on every rank)."""
+def model_of(name: str) -> str:
+    return MODEL_OF[name.split("[")[0]]
+
+
+def decode_workload(name: str, batch=None):
+    """
+    Host-side metadata of a decode-step workload (identical on every rank).
+    ``batch`` (profiling only) keeps the first sequences of the config's seeded
+    lengths with a pool sized for them, e.g. a few-GB slice of config 5.
+    """
     from tests import cases
     if name == "cfg2":
         meta = cases.config2_meta(0)
         return dict(name="cfg2", B=64, Hq=32, Hkv=8, D=128, NB=meta["num_blocks"],
                     ctx=meta["ctx"], tables=meta["tables"])
     if name == "cfg5":
-        meta = cases.config5_meta(0)
-        return dict(name="cfg5", B=256, Hq=64, Hkv=8, D=128, NB=meta["num_blocks"],
-                    ctx=meta["ctx"], tables=meta["tables"])
+        B = batch or 256
+        meta = cases.config5_meta(0, batch=B)
+        return dict(name="cfg5" if B == 256 else f"cfg5[:{B}]", B=B, Hq=64, Hkv=8, D=128,
+                    NB=meta["num_blocks"], ctx=meta["ctx"], tables=meta["tables"])
     raise ValueError(name)
 
 
@@ -696,7 +705,7 @@ def run_reference(args):
            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
            "data": "synthetic (seeded)",
            "config": {"workload": f"BASELINE {w['name']}: KV write + decode, "
-                                  f"{MODEL_OF[w['name']]} attention (Hq {w['Hq']}, Hkv {w['Hkv']}, "
+                                  f"{model_of(w['name'])} attention (Hq {w['Hq']}, Hkv {w['Hkv']}, "
                                   f"D {w['D']}), block 16",
                       "batch_per_step": 1, "sample": "one sequence per step (see cpu_baseline)"},
            "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": os.cpu_count(),
@@ -1032,7 +1041,7 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
 
-    w = decode_workload(args.workload)
+    w = decode_workload(args.workload, args.batch)
     st, r = bench_decode_step(args, w, world, rank, local, dev, with_clocks=(rank == 0))
     e2e = run_e2e(args, st, world, rank, dev)
     st.close()
@@ -1047,7 +1056,7 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded; random-init pool)",
             "config": {"workload": f"BASELINE {w['name']}: KV write + decode, "
-                                   f"{MODEL_OF[w['name']]} attention (Hq {w['Hq']}, "
+                                   f"{model_of(w['name'])} attention (Hq {w['Hq']}, "
                                    f"Hkv {w['Hkv']}, D {w['D']}), block 16",
                        "batch": w["B"], "kv_heads_per_gpu": w["Hkv"] // world,
                        "sum_ctx": int(w["ctx"].sum()), "pool_blocks": w["NB"],
@@ -1096,6 +1105,8 @@ def main():
     ap.add_argument("--soak-seconds", type=float, default=1.5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="profiling only: the first N sequences of config 5")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -301,6 +301,70 @@ MF_API int mf_commit_window(const void* win_k, const void* win_v, mf_dtype src_d
                      int32_t head_dim, int32_t* err_flag, mf_stream_t stream);
 
 /*
+ * accept_commit — a speculative round's acceptance decision and the commit of
+ * its confirmed prefix, fused into one launch.
+ *
+ * Replaces, per round, the reference's RejectionSampler.verify_tokens
+ * (memforge_ml/speculative/rejection_sampler.py:28-84, reached through
+ * resolve_round, memforge_ml/runtime/batched_speculative.py:731-777) followed
+ * by scatter_accepted_kv (:780-811).  For sequence b with K = num_drafts draft
+ * tokens x_0..x_{K-1}:
+ *   - greedy mode (target_probs == NULL): draft i is accepted while
+ *     x_i == target_tokens[b][i] (the target's argmax at candidate slot i);
+ *     next_token[b] = target_tokens[b][a];
+ *   - sampling mode: draft i is accepted while uniforms[b][i] <=
+ *     min(1, p_i / (q_i + 1e-9)), p_i = target_probs[b][i][x_i],
+ *     q_i = draft_probs[b][i][x_i]; next_token[b] is drawn at
+ *     resample_uniform[b] (inverse CDF, vocabulary order) from
+ *     max(0, p_a - q_a) renormalised (p_a when that is all zero) if a < K, or
+ *     from p_K (the bonus) if every draft was accepted;
+ *   a = the number of leading accepted drafts, written to num_accepted[b].
+ * When win_k is given, window rows 0..a of sequence b (the last confirmed token
+ * plus the accepted drafts; element (l, b*(K+1)+j, h, d) at
+ * win_k + l*win_stride_layer + (b*(K+1)+j)*win_stride_row + h*win_stride_head + d)
+ * are written at positions ctx_lens[b]+j of every layer, exactly as
+ * mf_commit_window with num_confirmed = a + 1 (same validation and error bits;
+ * window and pool share the element type, elem_bytes 2 or 4).  Rejected slots
+ * keep their contents.  All inputs live on the device: a round (verify
+ * attention, the target's softmax, this call) can be one CUDA graph.
+ * Probabilities are fp32 [seq][slot][vocab] with the given strides (vocab
+ * contiguous); token ids int32.
+ */
+typedef struct {
+  uint32_t struct_size;        /* sizeof(mf_accept_args) */
+  int32_t num_seqs, num_drafts;
+  const int32_t* draft_tokens; /* [num_seqs][draft_tokens_stride] */
+  int64_t draft_tokens_stride;
+  const int32_t* target_tokens; /* greedy: [num_seqs][target_tokens_stride], K+1 used */
+  int64_t target_tokens_stride;
+  const float* target_probs;   /* sampling: [num_seqs][K+1][vocab] or NULL (greedy) */
+  int64_t tp_stride_seq, tp_stride_slot;
+  const float* draft_probs;    /* sampling: [num_seqs][K][vocab] */
+  int64_t dp_stride_seq, dp_stride_slot;
+  int32_t vocab;
+  const float* uniforms;       /* sampling: [num_seqs][uniforms_stride], K used */
+  int64_t uniforms_stride;
+  const float* resample_uniform; /* sampling: [num_seqs] */
+  int32_t* num_accepted;       /* out: [num_seqs] */
+  int32_t* next_token;         /* out: [num_seqs] or NULL */
+  /* commit (optional: win_k == NULL decides only) */
+  const void* win_k;
+  const void* win_v;
+  int64_t win_stride_layer, win_stride_row, win_stride_head;
+  void* key_pool;
+  void* value_pool;
+  int64_t pool_stride_layer, pool_stride_block, pool_stride_slot, pool_stride_head;
+  int32_t num_layers, num_blocks, block_size;
+  const int32_t* block_tables; /* [num_seqs][table_stride] */
+  int32_t table_stride;
+  const int32_t* ctx_lens;     /* [num_seqs] */
+  int32_t num_kv_heads, head_dim, elem_bytes;
+  int32_t* err_flag;
+} mf_accept_args;
+
+MF_API int mf_accept_commit(const mf_accept_args* args, mf_stream_t stream);
+
+/*
  * Copy-on-write block copy across all layers: for each pair i, block
  * src[i] -> dst[i] in every layer of both pools (prefix_sharing.copy_block,
  * memforge_ml/runtime/prefix_sharing.py:28-42).  Pools are contiguous

@@ -37,7 +37,8 @@ _retired: list = []   # grown-out workspaces, kept alive for graphs that capture
 _err_words: Dict[int, torch.Tensor] = {}
 _checks = os.environ.get("MEMFORGE_CHECK", "0") not in ("", "0")
 launch_counter = {"reshape_and_cache": 0, "paged_attention": 0, "copy_blocks": 0,
-                  "peer_barrier": 0, "commit_window": 0, "gather_kv": 0}
+                  "peer_barrier": 0, "commit_window": 0, "gather_kv": 0,
+                  "accept_commit": 0}
 
 
 def set_checks(enabled: bool) -> None:

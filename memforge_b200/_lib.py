@@ -45,7 +45,7 @@ EXPORTED = (
     "mf_abi_version", "mf_last_error", "mf_device_info", "mf_reshape_and_cache",
     "mf_paged_attention_workspace_size", "mf_paged_attention", "mf_paged_decode",
     "mf_copy_blocks", "mf_paged_decode_noalloc", "mf_peer_barrier", "mf_ipc_export",
-    "mf_ipc_open", "mf_ipc_close", "mf_commit_window", "mf_gather_kv",
+    "mf_ipc_open", "mf_ipc_close", "mf_commit_window", "mf_gather_kv", "mf_accept_commit",
 )
 
 MF_IPC_HANDLE_BYTES = 64
@@ -74,6 +74,32 @@ class AttentionArgs(ctypes.Structure):
         ("scale", c_f32), ("causal", c_i32), ("dtype", ctypes.c_int),
         ("num_out_peers", c_i32), ("out_head_offset", c_i32),
         ("out_peers", c_vp * MF_MAX_OUT_PEERS),
+    ]
+
+
+class AcceptArgs(ctypes.Structure):
+    """Mirror of ``mf_accept_args``."""
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("num_seqs", c_i32), ("num_drafts", c_i32),
+        ("draft_tokens", c_vp), ("draft_tokens_stride", c_i64),
+        ("target_tokens", c_vp), ("target_tokens_stride", c_i64),
+        ("target_probs", c_vp), ("tp_stride_seq", c_i64), ("tp_stride_slot", c_i64),
+        ("draft_probs", c_vp), ("dp_stride_seq", c_i64), ("dp_stride_slot", c_i64),
+        ("vocab", c_i32),
+        ("uniforms", c_vp), ("uniforms_stride", c_i64),
+        ("resample_uniform", c_vp),
+        ("num_accepted", c_vp), ("next_token", c_vp),
+        ("win_k", c_vp), ("win_v", c_vp),
+        ("win_stride_layer", c_i64), ("win_stride_row", c_i64), ("win_stride_head", c_i64),
+        ("key_pool", c_vp), ("value_pool", c_vp),
+        ("pool_stride_layer", c_i64), ("pool_stride_block", c_i64),
+        ("pool_stride_slot", c_i64), ("pool_stride_head", c_i64),
+        ("num_layers", c_i32), ("num_blocks", c_i32), ("block_size", c_i32),
+        ("block_tables", c_vp), ("table_stride", c_i32),
+        ("ctx_lens", c_vp),
+        ("num_kv_heads", c_i32), ("head_dim", c_i32), ("elem_bytes", c_i32),
+        ("err_flag", c_vp),
     ]
 
 
@@ -106,6 +132,7 @@ def _declare(lib):
     lib.mf_gather_kv.argtypes = [
         c_vp, c_vp, ctypes.c_int, c_i64, c_i64, c_i64, c_i32, c_i32, c_vp, c_i32, c_i32, c_i32,
         c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_vp]
+    lib.mf_accept_commit.argtypes = [ctypes.POINTER(AcceptArgs), c_vp]
     lib.mf_copy_blocks.argtypes = [c_vp, c_vp, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp, c_vp]
     lib.mf_commit_window.argtypes = [
         c_vp, c_vp, ctypes.c_int, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, c_vp, c_vp,

@@ -325,16 +325,20 @@ def paged_mask(batch_size: int, q_length: int, kv_length: int, q_offset: int = 0
 # ---------------------------------------------------------- registration
 
 def register() -> bool:
-    """Add the function and its mask hook to the transformers registries (idempotent)."""
+    """
+    Add the function and its mask hook to the transformers registries
+    (idempotent).  Both go into the library-wide mappings (``register``), which
+    is where mask creation looks an implementation up.
+    """
     try:
         from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS
         from transformers.modeling_utils import ALL_ATTENTION_FUNCTIONS
     except ImportError:
         return False
-    if BACKEND_NAME not in ALL_ATTENTION_FUNCTIONS:
-        ALL_ATTENTION_FUNCTIONS[BACKEND_NAME] = paged_attention_forward
-    if BACKEND_NAME not in ALL_MASK_ATTENTION_FUNCTIONS:
-        ALL_MASK_ATTENTION_FUNCTIONS[BACKEND_NAME] = paged_mask
+    if ALL_ATTENTION_FUNCTIONS._global_mapping.get(BACKEND_NAME) is not paged_attention_forward:
+        ALL_ATTENTION_FUNCTIONS.register(BACKEND_NAME, paged_attention_forward)
+    if ALL_MASK_ATTENTION_FUNCTIONS._global_mapping.get(BACKEND_NAME) is not paged_mask:
+        ALL_MASK_ATTENTION_FUNCTIONS.register(BACKEND_NAME, paged_mask)
     return True
 
 

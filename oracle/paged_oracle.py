@@ -351,3 +351,72 @@ def standalone_paged_attention(query: np.ndarray, key_cache: np.ndarray,
     o = np.matmul(p, values)               # (H, q, D)
     H, qlen, D = o.shape
     return np.transpose(o, (1, 0, 2)).reshape(1, qlen, H * D)
+
+
+# --------------------------------------------------------------------------
+# (f3) speculative acceptance — integer decision, exact given the uniforms
+# --------------------------------------------------------------------------
+
+
+def accepted_drafts(draft_tokens: Sequence[int], target_probs: Optional[np.ndarray] = None,
+                    draft_probs: Optional[np.ndarray] = None,
+                    uniforms: Optional[Sequence[float]] = None,
+                    target_tokens: Optional[Sequence[int]] = None) -> int:
+    """
+    Number of leading accepted drafts of one sequence.
+
+    Sampling (``RejectionSampler.verify_tokens``, ``rejection_sampler.py:46-66``):
+    draft i is accepted when ``r_i <= min(1, p(x_i) / (q(x_i) + 1e-9))`` with the
+    reference's Python-float (double) arithmetic; the uniforms ``r_i`` are given
+    instead of drawn.  Greedy (temperature 0, ``batched_speculative.py:744-757``):
+    point-mass distributions, so draft i is accepted while it equals the target's
+    argmax at slot i.
+    """
+    n = 0
+    for i, x in enumerate(draft_tokens):
+        x = int(x)
+        if target_probs is None:
+            ok = x == int(target_tokens[i])
+        else:
+            p = float(target_probs[i][x])
+            q = float(draft_probs[i][x])
+            ok = float(uniforms[i]) <= min(1.0, p / (q + 1e-9))
+        if not ok:
+            break
+        n += 1
+    return n
+
+
+def inverse_cdf_draw(weights: np.ndarray, u: float) -> Optional[int]:
+    """
+    Token drawn from unnormalised non-negative ``weights`` at uniform ``u``: the
+    smallest v with ``cumsum(weights)[v] > u * sum(weights)`` (float64), or None
+    when the weights sum to zero.  ``sample_from_probs``
+    (``rejection_sampler.py:13-26``) draws from the same distribution with
+    ``torch.multinomial``; a given ``u`` makes the draw reproducible.
+    """
+    w = np.maximum(np.asarray(weights, dtype=np.float64), 0.0)
+    total = w.sum()
+    if not total > 0:
+        return None
+    c = np.cumsum(w)
+    return int(min(np.searchsorted(c, u * total, side="right"), len(w) - 1))
+
+
+def next_token_after(accepted: int, num_drafts: int, target_probs: np.ndarray,
+                     draft_probs: np.ndarray, u: float) -> int:
+    """
+    The token that follows the accepted drafts (``rejection_sampler.py:67-84``):
+    after a rejection at slot a, a draw from ``clamp(p_a - q_a, 0)`` (from
+    ``p_a`` when that is all zero); after all K accepted, the bonus draw from
+    ``p_K``.
+    """
+    if accepted < num_drafts:
+        tok = inverse_cdf_draw(target_probs[accepted] - draft_probs[accepted], u)
+        if tok is None:
+            tok = inverse_cdf_draw(target_probs[accepted], u)
+    else:
+        tok = inverse_cdf_draw(target_probs[num_drafts], u)
+    if tok is None:
+        tok = min(len(target_probs[0]) - 1, int(u * len(target_probs[0])))
+    return tok

@@ -20,6 +20,7 @@ Reference functions exercised (paths inside the reference):
   memforge_ml/kernels/block_attention.py   paged_attention_blockwise
   memforge_ml/models/paged_attention.py    PagedKVCache, PagedAttention
   memforge_ml/runtime/batched_speculative.py  scatter_accepted_kv
+  memforge_ml/speculative/rejection_sampler.py RejectionSampler.verify_tokens
 """
 
 from __future__ import annotations
@@ -274,6 +275,45 @@ def gen_commit(out):
                         block_size=BS, **res)
 
 
+def gen_accept(out):
+    """
+    RejectionSampler.verify_tokens on seeded draft/target distributions.  Its
+    uniforms come from torch.rand(1), one per examined draft, after
+    torch.manual_seed(seed): the same calls replayed after the same seed give
+    the values it compared against (stored as `uniforms`), so the acceptance
+    count is reproducible from them.  The draws after the decision
+    (torch.multinomial) are recorded to check which distribution they come from.
+    """
+    import torch
+    from memforge_ml.speculative.rejection_sampler import RejectionSampler
+    g = cases.rng(70)
+    K, V, cases_n = 4, 12, 64
+    res = {"draft": [], "p": [], "q": [], "uniforms": [], "accepted": [], "last_token": [],
+           "last_is_draft": []}
+    for c in range(cases_n):
+        q = g.dirichlet(np.ones(V) * 0.5, size=K).astype(np.float32)
+        p = g.dirichlet(np.ones(V) * 0.5, size=K + 1).astype(np.float32)
+        if c % 4 == 0:   # drafts the target agrees with: long accepted runs
+            p[:K] = 0.6 * q + 0.4 * p[:K]
+        draft = np.array([g.choice(V, p=q[i] / q[i].sum()) for i in range(K)], np.int32)
+        seed = 1000 + c
+        torch.manual_seed(seed)
+        toks, is_draft, n = RejectionSampler.verify_tokens(
+            [int(x) for x in draft], [torch.from_numpy(q[i]) for i in range(K)],
+            [torch.from_numpy(p[i]) for i in range(K + 1)])
+        torch.manual_seed(seed)
+        r = np.array([torch.rand(1).item() for _ in range(K)], np.float32)
+        res["draft"].append(draft)
+        res["p"].append(p)
+        res["q"].append(q)
+        res["uniforms"].append(r)
+        res["accepted"].append(n)
+        res["last_token"].append(toks[-1] if toks else -1)
+        res["last_is_draft"].append(bool(is_draft[-1]) if is_draft else True)
+    np.savez_compressed(os.path.join(out, "accept.npz"),
+                        **{k: np.asarray(v) for k, v in res.items()})
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -287,6 +327,7 @@ def main():
     gen_config1(HERE)
     gen_standalone(HERE)
     gen_commit(HERE)
+    gen_accept(HERE)
     print("golden fixtures written to", HERE)
 
 

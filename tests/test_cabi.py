@@ -38,14 +38,16 @@ def test_every_declared_symbol_is_exported():
     assert exported == set(syms)
 
 
-def test_args_struct_layout_matches_the_header():
-    """sizeof and offsets of mf_attention_args agree between C and ctypes."""
-    fields = [f for f, _ in L.AttentionArgs._fields_]
+@pytest.mark.parametrize("cname,struct", [("mf_attention_args", L.AttentionArgs),
+                                          ("mf_accept_args", L.AcceptArgs)])
+def test_args_struct_layout_matches_the_header(cname, struct):
+    """sizeof and offsets of the argument structs agree between C and ctypes."""
+    fields = [f for f, _ in struct._fields_]
     src = ["#include <stdio.h>", "#include <stddef.h>", '#include "memforge_sm100.h"',
            "int main(void){",
-           'printf("%zu\\n", sizeof(mf_attention_args));']
+           f'printf("%zu\\n", sizeof({cname}));']
     for f in fields:
-        src.append(f'printf("%zu\\n", offsetof(mf_attention_args, {f}));')
+        src.append(f'printf("%zu\\n", offsetof({cname}, {f}));')
     src.append("return 0;}")
     with tempfile.TemporaryDirectory() as d:
         c = os.path.join(d, "t.c")
@@ -54,9 +56,9 @@ def test_args_struct_layout_matches_the_header():
         subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
         vals = [int(x) for x in subprocess.run([exe], capture_output=True, text=True,
                                                check=True).stdout.split()]
-    assert vals[0] == ctypes.sizeof(L.AttentionArgs)
+    assert vals[0] == ctypes.sizeof(struct)
     for f, off in zip(fields, vals[1:]):
-        assert getattr(L.AttentionArgs, f).offset == off, f
+        assert getattr(struct, f).offset == off, f
 
 
 def test_error_paths_without_a_gpu():

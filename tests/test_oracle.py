@@ -243,3 +243,42 @@ def test_oracle_rejects_like_the_reference():
     with pytest.raises(ValueError, match="not a multiple of"):
         O.varlen_attention(np.zeros((3, 1, 8), np.float32), c.k_pool[None], c.v_pool[None], 0,
                            [c.tables[0]], [0], [7], 16)
+
+
+def test_acceptance_rule_matches_reference_verify_tokens(golden_dir):
+    """accepted_drafts reproduces RejectionSampler.verify_tokens's accepted count from
+    the uniforms it drew, and the token it drew afterwards has positive weight under
+    the distribution next_token_after draws from."""
+    f = np.load(os.path.join(golden_dir, "accept.npz"))
+    K = f["draft"].shape[1]
+    seen = set()
+    for c in range(f["draft"].shape[0]):
+        p, q = f["p"][c].astype(np.float64), f["q"][c].astype(np.float64)
+        n = O.accepted_drafts(f["draft"][c], f["p"][c], f["q"][c], f["uniforms"][c])
+        assert n == int(f["accepted"][c]), c
+        seen.add(n)
+        if n < K:
+            w = np.maximum(p[n] - q[n], 0.0)
+            if w.sum() == 0:
+                w = p[n]
+        else:
+            w = p[K]
+        assert w[int(f["last_token"][c])] > 0, c
+        assert not bool(f["last_is_draft"][c])
+    assert seen == set(range(K + 1))     # every outcome 0..K occurs
+
+
+def test_greedy_acceptance_and_inverse_cdf_draw():
+    assert O.accepted_drafts([3, 4, 9], target_tokens=[3, 4, 1, 7]) == 2
+    assert O.accepted_drafts([3, 4], target_tokens=[3, 4, 8]) == 2
+    assert O.accepted_drafts([5], target_tokens=[3, 1]) == 0
+    w = np.array([0.0, 1.0, 0.0, 3.0])
+    assert O.inverse_cdf_draw(w, 0.0) == 1
+    assert O.inverse_cdf_draw(w, 0.24) == 1
+    assert O.inverse_cdf_draw(w, 0.26) == 3
+    assert O.inverse_cdf_draw(np.zeros(4), 0.5) is None
+    p = np.array([[0.5, 0.5, 0.0], [0.0, 0.0, 1.0]])
+    q = np.array([[0.5, 0.5, 0.0]])
+    # rejection at 0 with p == q: the difference is all zero, so the draw is from p
+    assert O.next_token_after(0, 1, p, q, 0.75) == 1
+    assert O.next_token_after(1, 1, p, q, 0.1) == 2
