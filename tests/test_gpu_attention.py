@@ -121,8 +121,16 @@ def test_multi_row_causal_from_pool(W):
     check(c)
 
 
-def test_long_rows_use_the_generic_kernel():
+def test_long_bf16_rows_take_the_prefill_kernel():
+    """160 rows per kv head (G 4 x 40 positions): dispatched to the tcgen05 prefill kernel."""
     c = cases.small_decode_case("long", 14, "bf16", 32, 8, 128, [70, 300], q_per_seq=40)
+    check(c)
+
+
+@pytest.mark.parametrize("q_per_seq", [1, 3, 40])
+def test_bf16_head_dim_80_takes_the_generic_kernel(q_per_seq):
+    """head_dim 80 is served by neither tensor-core kernel: the generic CUDA-core kernel, bf16."""
+    c = cases.small_decode_case("gen80", 15, "bf16", 12, 4, 80, [40, 50, 333], q_per_seq=q_per_seq)
     check(c)
 
 
