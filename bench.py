@@ -746,7 +746,11 @@ def _time_each(fn, steps, warmup, dev):
 
 
 def extra_cfg2(args, dev):
-    """Config 2 (Llama-3-8B, 64 sequences): the decode step, its roofline."""
+    """
+    Config 2 (Llama-3-8B, 64 sequences).  The roofline's kernel time comes from
+    steps timed as two graphs with events around the decode; the step value is
+    the same step as one graph, where the decode starts while the write ends.
+    """
     import torch
     w = decode_workload("cfg2")
     st, r = bench_decode_step(args, w, 1, 0, dev.index, dev, with_clocks=False)
@@ -758,11 +762,14 @@ def extra_cfg2(args, dev):
     torch.cuda.empty_cache()
     return {"workload": "BASELINE cfg2: KV write + decode, Llama-3-8B (Hq 32, Hkv 8, D 128), "
                         "64 sequences, ctx ~U[256,4096], 16384-block pool",
-            "value": round(r["value"], 2), "unit": "GB/s", "ms_per_step": round(r["ms_per_step"], 5),
-            "one_graph_ms_per_step": round(one_ms, 5),
-            "one_graph_value": round((attn_b + write_b) / (one_ms * 1e-3) / 1e9, 2),
+            "value": round((attn_b + write_b) / (one_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(one_ms, 5),
+            "launch": "the step as one CUDA graph (the decode a programmatic dependent launch of "
+                      "the write)",
+            "two_graph_ms_per_step": round(r["ms_per_step"], 5),
+            "two_graph_value": round(r["value"], 2),
             "roofline": r["roofline"], "validated": r["validated"],
-            "attn_tokens_per_s": round(64 / (r["ms_per_step"] * 1e-3), 1)}
+            "attn_tokens_per_s": round(64 / (one_ms * 1e-3), 1)}
 
 
 def extra_cfg2_layers(args, dev, layers=32):
