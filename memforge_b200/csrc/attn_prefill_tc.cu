@@ -26,6 +26,12 @@
 // again as soon as the softmax warps have loaded it: the S of a tile can be
 // computed while the softmax of the previous tile runs.
 //
+// Each lane quarter has two softmax warps that take alternate key tiles, so one
+// warp's TMEM load, row max and P store overlap the other's exponentials.  An
+// item's epilogue (combining the two warps' row sums, normalising O, storing)
+// is deferred past each warp's first tile of the next item, so the tensor pipe
+// is not idle while O is read out.
+//
 // The online softmax keeps a per-row reference max (log2 units) and only
 // rescales O (a TMEM read-modify-write) when a tile's max exceeds it by more
 // than 2^8, so the exponentials stay <= 256 and the correction is rare after the
@@ -45,12 +51,14 @@ namespace pf {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int WPQ = 1;                  // softmax warps per TMEM lane quarter
+constexpr int WPQ = 2;                  // softmax warps per TMEM lane quarter (tile parities)
 constexpr int SM_WARPS = 4 * WPQ;       // softmax warps
-constexpr int CW = BN / WPQ;            // score columns per softmax warp
+constexpr int TILE_WARPS = 4;           // softmax warps working on one tile (one per quarter)
+constexpr int CW = BN;                  // score columns per softmax warp (all of its tiles)
 constexpr int TMA_WARP = SM_WARPS, V_WARP = SM_WARPS + 1, MMA_WARP = SM_WARPS + 2,
               PV_WARP = SM_WARPS + 3;
 constexpr int THREADS = (SM_WARPS + 4) * 32;
+
 static_assert(CW == 32 || CW == 64 || CW == 128, "softmax column split");
 constexpr int D = 128;
 constexpr int PAGE = 16;
@@ -77,15 +85,17 @@ constexpr int B_QFULL = 0, B_QEMPTY = 2, B_KFULL = 4, B_VFULL = B_KFULL + KS,
               B_SDONE = B_VFULL + KS, B_SFREE = B_SDONE + 2, B_PFULL = B_SFREE + 2,
               B_PVDONE = B_PFULL + 2,
               B_OFULL = B_PVDONE + 2, B_OFREE = B_OFULL + 1, B_IDLE = B_OFREE + 1,
-              B_XCH = B_IDLE + 1, NBAR = B_XCH + 4;
+              B_HAND = B_IDLE + 1, B_EXL = B_HAND + 8, NBAR = B_EXL + 4;
 constexpr uint32_t OFF_MISC = OFF_BAR + NBAR * 8;  // TMEM base, abort flag
-// Row-statistic exchange between the softmax warps of a lane quarter: two
-// buffers of [WPQ][BM] floats.
+// Row statistics passed between the two softmax warps of a lane quarter:
+// m[2 parities][BM] (the reference max after a tile), then l[2 items][2
+// parities][BM] and ms[2 items][2 parities][BM] (an item's partial row sums and
+// the reference max they are scaled to).
 constexpr uint32_t OFF_XCH = OFF_MISC + 16;
 // Work-list tables: prefix int[num_seqs + 1] (query tiles before the k-th
 // sequence in longest-first order), order uint16[num_seqs] (that sequence), and
 // NBK bucket counters of the counting sort.
-constexpr uint32_t OFF_PREFIX = OFF_XCH + 2 * WPQ * BM * 4;
+constexpr uint32_t OFF_PREFIX = OFF_XCH + 10 * BM * 4;
 constexpr int NBK = 256;
 
 // TMEM column offsets
@@ -203,8 +213,8 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
       mbar_init(&bar[B_QFULL + i], 1);
       mbar_init(&bar[B_QEMPTY + i], 1);
       mbar_init(&bar[B_SDONE + i], 1);
-      mbar_init(&bar[B_SFREE + i], SM_WARPS);
-      mbar_init(&bar[B_PFULL + i], SM_WARPS);
+      mbar_init(&bar[B_SFREE + i], TILE_WARPS);
+      mbar_init(&bar[B_PFULL + i], TILE_WARPS);
       mbar_init(&bar[B_PVDONE + i], 1);
     }
     for (int st = 0; st < KS; ++st) {
@@ -212,9 +222,10 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
       mbar_init(&bar[B_VFULL + st], 1);
     }
     mbar_init(&bar[B_OFULL], 1);
-    mbar_init(&bar[B_OFREE], SM_WARPS);
+    mbar_init(&bar[B_OFREE], SM_WARPS);  // every softmax warp reads its half of O
     mbar_init(&bar[B_IDLE], 2);  // one commit per issuer
-    for (int q = 0; q < 4; ++q) mbar_init(&bar[B_XCH + q], WPQ);
+    for (int i = 0; i < 8; ++i) mbar_init(&bar[B_HAND + i], 1);
+    for (int q = 0; q < 4; ++q) mbar_init(&bar[B_EXL + q], WPQ);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -491,33 +502,72 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
     }
   } else {
     // ====================================== softmax (warps 0 .. SM_WARPS-1)
-    const int quarter = warp & 3, cs = warp >> 2;
+    // Two warps per TMEM lane quarter: the warp of parity par = warp / 4 takes
+    // the tiles whose global index g has g % 2 == par (S buffer par, P buffer
+    // par), so one warp's TMEM load, row max and P store overlap the other's
+    // exponentials.  The online softmax is sequential only in its reference
+    // max: a warp finishes its tile's row max, then takes the previous tile's
+    // reference max from the other warp (mbox, B_HAND), decides its own,
+    // publishes it, and only then computes the exponentials.  Each warp keeps
+    // its own row sums, scaled to the reference max it last saw; at an item's
+    // end the two partial sums are combined (l / ms boxes, B_EXL) and each
+    // warp normalises and stores half of O's columns.
+    const int quarter = warp & 3, par = warp >> 2;
     const int row = quarter * 32 + lane;  // TMEM lane == tile row
-    const int col0 = cs * CW;             // this warp's columns of S / O
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tO = tmem + COL_O + lane_off + col0;
-    float* xch = reinterpret_cast<float*>(gbase + OFF_XCH);
+    const uint32_t tO = tmem + COL_O + lane_off;
+    float* mbox = reinterpret_cast<float*>(gbase + OFF_XCH);  // [2][BM]
+    float* lbox = mbox + 2 * BM;                               // [2 items][2][BM]
+    float* msbox = lbox + 4 * BM;                              // [2 items][2][BM]
     const float sl2 = P.scale_log2;
     bool ok = true;
-    uint32_t xc = 0;  // exchanges done by this warp
-    // Combine one per-row value over the WPQ warps of this lane quarter (max
-    // or sum); false (on every lane) when the bounded wait gave up.
-    auto exchange = [&](float v, bool is_max, float& out) -> bool {
-      if (WPQ == 1) {
-        out = v;
-        return true;
-      }
-      float* buf = xch + (xc & 1) * WPQ * BM;
-      buf[cs * BM + row] = v;
+    // An item's epilogue runs after this warp's first tile of the next item
+    // (or at the next item's end when it has none): by then the item's last
+    // P V has completed and the other warp has finished the item too, so
+    // neither the O wait nor the row-sum exchange stalls, and the next item's
+    // first tiles run meanwhile.  Its first P V waits for O to be read.
+    bool pend = false;
+    int pend_ic = 0;
+    bool pend_valid = false;
+    T* pend_row = nullptr;
+    float pend_l = 0.f, pend_m = -INFINITY;
+    auto epilogue = [&]() -> bool {
+      float* lb = lbox + (pend_ic & 1) * 2 * BM;
+      float* mb = msbox + (pend_ic & 1) * 2 * BM;
+      lb[par * BM + row] = pend_l;
+      mb[par * BM + row] = pend_m;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_XCH + quarter]);
-      const bool fine = mbar_wait_bounded(&bar[B_XCH + quarter], xc & 1, WAIT_LIMIT);
-      ++xc;
-      if (__any_sync(0xffffffffu, !fine)) return false;
-      float r = buf[row];
+      if (lane == 0) mbar_arrive(&bar[B_EXL + quarter]);
+      bool done = mbar_wait_bounded(&bar[B_EXL + quarter], pend_ic & 1, WAIT_LIMIT);
+      const float l_oth = lb[(par ^ 1) * BM + row], m_oth = mb[(par ^ 1) * BM + row];
+      const float m_fin = fmaxf(pend_m, m_oth);
+      float l_tot = 0.f;
+      if (pend_m != -INFINITY) l_tot += pend_l * fast_exp2(pend_m - m_fin);
+      if (m_oth != -INFINITY) l_tot += l_oth * fast_exp2(m_oth - m_fin);
+      done = done && !*abort_flag && mbar_wait_bounded(&bar[B_OFULL], pend_ic & 1, WAIT_LIMIT);
+      done = __all_sync(0xffffffffu, done);
+      if (!done) return false;
+      tc_fence_after();
+      uint32_t o[64];
+      tmem_ld32(tO + par * 64, o);
+      tmem_ld32(tO + par * 64 + 32, o + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_OFREE]);  // O may be overwritten
+      if (pend_valid) {
+        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
 #pragma unroll
-      for (int k = 1; k < WPQ; ++k) r = is_max ? fmaxf(r, buf[k * BM + row]) : r + buf[k * BM + row];
-      out = r;
+        for (int e = 0; e < 64; e += 8) {
+          uint4 v;
+          v.x = Mma<T>::pack(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+          v.y = Mma<T>::pack(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+          v.z = Mma<T>::pack(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+          v.w = Mma<T>::pack(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+          *reinterpret_cast<uint4*>(pend_row + e) = v;
+        }
+      }
+      pend = false;
       return true;
     };
     uint32_t g = 0;
@@ -530,10 +580,11 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
       // Last visible key: causal over the context; with a window, every pool key
       // and, in the window tile, window keys 0..pos.
       const int limit = P.window ? I.pool_len - 1 : min(I.win_start + pos, I.kv_len - 1);
-      float m_ref = -INFINITY, l_sum = 0.f;
+      float m_seen = -INFINITY;  // reference max l_own is scaled to
+      float l_own = 0.f;
       for (int j = 0; j < I.nt; ++j, ++g) {
-        const int sb = g & 1, pb = g & 1;
-        if (!mbar_wait_bounded(&bar[B_SDONE + sb], (g >> 1) & 1, WAIT_LIMIT)) ok = false;
+        if ((int)(g & 1) != par) continue;  // the other warp's tile
+        if (!mbar_wait_bounded(&bar[B_SDONE + par], (g >> 1) & 1, WAIT_LIMIT)) ok = false;
         // Warp-uniform decision: tcgen05.ld/st below are warp-collective.
         if (__any_sync(0xffffffffu, !ok || *abort_flag != 0)) {
           ok = false;
@@ -543,46 +594,96 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         float sv[CW];
 #pragma unroll
         for (int c = 0; c < CW / 32; ++c)
-          tmem_ld32(tmem + COL_S + sb * 128 + lane_off + col0 + c * 32,
+          tmem_ld32(tmem + COL_S + par * 128 + lane_off + c * 32,
                     reinterpret_cast<uint32_t*>(sv + c * 32));
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[B_SFREE + sb]);  // S buffer may be overwritten
+        if (lane == 0) mbar_arrive(&bar[B_SFREE + par]);  // S buffer may be overwritten
 
-        // Row max of the raw scores over the visible columns (col0 + c <= limit).
+        // Row max of the raw scores over the visible columns (c <= limit).
         const bool win_tile = P.window && j == I.nt - 1;
-        const int lim = (win_tile ? pos : limit - j * BN) - col0;
+        const int lim = win_tile ? pos : limit - j * BN;
         if (__any_sync(0xffffffffu, lim < CW - 1)) {
 #pragma unroll
           for (int c = 0; c < CW; ++c)
             if (c > lim) sv[c] = -INFINITY;
         }
-        // Eight independent chains of three-input maxima (two new columns each).
         float mx[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) mx[e] = sv[e];
 #pragma unroll
         for (int c = 8; c < CW; c += 2) mx[(c >> 1) & 7] = fmax3f(mx[(c >> 1) & 7], sv[c], sv[c + 1]);
-        float mraw = fmax3f(fmax3f(mx[0], mx[1], mx[2]), fmax3f(mx[3], mx[4], mx[5]),
-                            fmaxf(mx[6], mx[7]));
-        if (!exchange(mraw, true, mraw)) {
+        const float mraw = fmax3f(fmax3f(mx[0], mx[1], mx[2]), fmax3f(mx[3], mx[4], mx[5]),
+                                  fmaxf(mx[6], mx[7]));
+        // The previous tile's reference max (the other warp's), unless this
+        // tile starts an item.
+        float m_prev = -INFINITY;
+        if (g > 0) {
+          if (!mbar_wait_bounded(&bar[B_HAND + quarter * 2 + (par ^ 1)], ((g - 1) >> 1) & 1,
+                                 WAIT_LIMIT))
+            ok = false;
+          if (j > 0) m_prev = mbox[(par ^ 1) * BM + row];
+        }
+        if (__any_sync(0xffffffffu, !ok)) {
           ok = false;
           break;
         }
+        // l_own follows every rescale the other warp decided.
+        if (m_prev != m_seen && m_seen != -INFINITY) l_own *= fast_exp2(m_seen - m_prev);
         // Lazy rescale: a row keeps its reference max unless this tile exceeds
-        // it by more than 2^8 (the same decision in every warp of the row).  The
-        // O correction is a warp-collective TMEM read-modify-write, done when
-        // any row of the warp needs it (the other rows multiply by 1).
+        // it by more than 2^8 (log2 units).
         const float tmax = mraw * sl2;
-        float f = 1.f;
+        float m_ref = m_prev, f = 1.f;
         if (mraw != -INFINITY && (m_ref == -INFINITY || tmax > m_ref + RESCALE_THRESHOLD)) {
           if (m_ref != -INFINITY) f = fast_exp2(m_ref - tmax);
           m_ref = tmax;
         }
-        l_sum *= f;
+        l_own *= f;
+        m_seen = m_ref;
+        mbox[par * BM + row] = m_ref;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar[B_HAND + quarter * 2 + par]);
+        // The P buffer is free once the P V product of two tiles ago completed.
+        if (g >= 2 && !mbar_wait_bounded(&bar[B_PVDONE + par], ((g >> 1) - 1) & 1, WAIT_LIMIT))
+          ok = false;
+        if (__any_sync(0xffffffffu, !ok)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // P = 2^(s * scale_log2 - m_ref), packed to 16-bit pairs and stored 32
+        // columns at a time (the scores of a stored chunk are dead, so their
+        // registers hold the next chunk's P); scaling and row sums as packed
+        // fp32 pairs, the exponentials on the SFU.
+        const float nmu = (m_ref == -INFINITY) ? 0.f : -m_ref;
+        const uint64_t sl2x2 = f32x2(sl2, sl2), nmux2 = f32x2(nmu, nmu);
+        uint64_t ps2[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
+        const uint32_t tp = tmem + COL_P + par * 64 + lane_off;
+#pragma unroll
+        for (int ch = 0; ch < CW / 32; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            float x0, x1;
+            const int col = ch * 32 + 2 * c;
+            f32x2_split(f32x2_fma(f32x2(sv[col], sv[col + 1]), sl2x2, nmux2), x0, x1);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            ps2[c & 1] = f32x2_add(ps2[c & 1], f32x2(p0, p1));
+            pk[c] = Mma<T>::pack(p0, p1);
+          }
+          tmem_st16(tp + ch * 16, pk);
+        }
+        float ps_lo, ps_hi;
+        f32x2_split(f32x2_add(ps2[0], ps2[1]), ps_lo, ps_hi);
+        l_own += ps_lo + ps_hi;
+        tmem_wait_st();
         if (j > 0 && __any_sync(0xffffffffu, f != 1.f)) {
-          // O must include P_{j-1} V_{j-1} before it is rescaled.
+          // O must include P_{g-1} V_{g-1} before it is rescaled, and the
+          // rescale must land before this tile's P V (ordered by P-full below).
+          // A pending epilogue goes first: P_{g-1} V_{g-1} may be this item's
+          // first P V, which waits for the previous item's O to be read.
+          if (pend && !epilogue()) ok = false;
           if (!mbar_wait_bounded(&bar[B_PVDONE + ((g - 1) & 1)], ((g - 1) >> 1) & 1, WAIT_LIMIT))
             ok = false;
           tc_fence_after();
@@ -595,52 +696,17 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
             tmem_st32(tO + c * 32, o);
           }
+          tmem_wait_st();
         }
-        // P = 2^(s * scale_log2 - m_ref), packed to 16-bit pairs.  The scaling
-        // and the row sums run as packed fp32 pairs (two columns per
-        // instruction), the exponentials on the SFU.
-        const float nmu = (m_ref == -INFINITY) ? 0.f : -m_ref;
-        const uint64_t sl2x2 = f32x2(sl2, sl2), nmux2 = f32x2(nmu, nmu);
-        uint64_t ps2[2] = {f32x2(0.f, 0.f), f32x2(0.f, 0.f)};
-        uint32_t pk[CW / 2];
-#pragma unroll
-        for (int c = 0; c < CW / 2; ++c) {
-          float x0, x1;
-          f32x2_split(f32x2_fma(f32x2(sv[2 * c], sv[2 * c + 1]), sl2x2, nmux2), x0, x1);
-          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-          ps2[c & 1] = f32x2_add(ps2[c & 1], f32x2(p0, p1));
-          pk[c] = Mma<T>::pack(p0, p1);
-        }
-        float ps_lo, ps_hi;
-        f32x2_split(f32x2_add(ps2[0], ps2[1]), ps_lo, ps_hi);
-        l_sum += ps_lo + ps_hi;
-        // The P buffer is free once the P V product of two tiles ago completed.
-        if (g >= 2 && !mbar_wait_bounded(&bar[B_PVDONE + pb], ((g >> 1) - 1) & 1, WAIT_LIMIT))
-          ok = false;
-        if (__any_sync(0xffffffffu, !ok)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t tp = tmem + COL_P + pb * 64 + lane_off + col0 / 2;
-        if constexpr (CW == 128) {
-          tmem_st32(tp, pk);
-          tmem_st32(tp + 32, pk + 32);
-        } else if constexpr (CW == 64) {
-          tmem_st32(tp, pk);
-        } else {
-          tmem_st16(tp, pk);
-        }
-        tmem_wait_st();
         const int kbase = j * BN;
         // Keys of this tile past the last one loaded: past the pool in the last
         // pool tile, past q_len in the window tile (whose other rows were never
         // written by this tile's loads).
         const int loaded = win_tile ? I.q_len : I.pool_len - kbase;
-        if (warp == 0 && loaded < BN) {
+        if (quarter == 0 && loaded < BN) {
           // Zero the V rows of those keys (whole 128-byte rows of both halves)
-          // so p = 0 adds nothing even where a slot holds NaN.  Warp 0's p_full
-          // arrival orders it before P V.
+          // so p = 0 adds nothing even where a slot holds NaN.  This warp's
+          // P-full arrival orders it before P V.
           const int st = g % KS;
           if (!mbar_wait_bounded(&bar[B_VFULL + st], (g / KS) & 1, WAIT_LIMIT)) ok = false;
           const uint32_t vb = base + OFF_V + st * TILE_BYTES;
@@ -654,48 +720,30 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bar[B_PFULL + pb]);
+        if (lane == 0) mbar_arrive(&bar[B_PFULL + par]);
+        if (pend && !epilogue()) {
+          ok = false;
+          break;
+        }
       }
       // Uniform: the epilogue below is warp-collective.
       if (__any_sync(0xffffffffu, !ok)) {
         ok = false;
         break;
       }
-      // ---------------------------------------------------------- epilogue
-      bool done = !*abort_flag && mbar_wait_bounded(&bar[B_OFULL], ic & 1, WAIT_LIMIT);
-      done = __all_sync(0xffffffffu, done);
-      if (!done) {
+      if (pend && !epilogue()) {  // no tile of this item was this warp's
         ok = false;
         break;
       }
-      tc_fence_after();
-      uint32_t o[CW];
-#pragma unroll
-      for (int c = 0; c < CW / 32; ++c) tmem_ld32(tO + c * 32, o + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_OFREE]);  // O may be overwritten
-      float l_tot;
-      if (!exchange(l_sum, false, l_tot)) {
-        ok = false;
-        break;
-      }
-      if (row_valid) {
-        const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
-        T* orow = static_cast<T*>(P.a.out) + (int64_t)(I.q_start + pos) * P.a.o_sr +
-                  (int64_t)(I.h * G + gg) * P.a.o_sh + col0;
-#pragma unroll
-        for (int e = 0; e < CW; e += 8) {
-          uint4 v;
-          v.x = Mma<T>::pack(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
-          v.y = Mma<T>::pack(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
-          v.z = Mma<T>::pack(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
-          v.w = Mma<T>::pack(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + e) = v;
-        }
-      }
+      pend = true;
+      pend_ic = ic;
+      pend_valid = row_valid;
+      pend_row = static_cast<T*>(P.a.out) + (int64_t)(I.q_start + (row_valid ? pos : 0)) * P.a.o_sr +
+                 (int64_t)(I.h * G + gg) * P.a.o_sh + par * 64;
+      pend_l = l_own;
+      pend_m = m_seen;
     }
+    if (ok && pend && !epilogue()) ok = false;
     if (!ok) {
       if (lane == 0) set_err(P.a.err, MF_ERR_TIMEOUT);
       *abort_flag = 1;
