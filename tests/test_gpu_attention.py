@@ -82,13 +82,31 @@ def test_config1_fp32():
     check(c)
 
 
-@pytest.mark.parametrize("hq,hkv,W", [(40, 8, 5), (64, 8, 5), (32, 8, 4), (16, 2, 3)])
+@pytest.mark.parametrize("hq,hkv,W", [(40, 8, 5), (64, 8, 5), (32, 8, 4), (16, 2, 3), (32, 2, 16)])
 def test_verify_window_matches_oracle(hq, hkv, W):
-    c = cases.small_decode_case("verify", 12, "bf16", hq, hkv, 128, [5, 200, 1000, 33], q_per_seq=W)
+    c = cases.small_decode_case("verify", 12, "bf16", hq, hkv, 128, [max(5, W), 200, 1000, 33],
+                                q_per_seq=W)
     g = cases.rng(12)
     window = {s: (int(c.ctx_lens[s]) - W, cases.bf16_round(cases.normal(g, (hkv, W, 128))),
                   cases.bf16_round(cases.normal(g, (hkv, W, 128)))) for s in range(c.batch)}
     check(c, window)
+
+
+def test_verify_split_merges_many_ranges_and_repeats():
+    """Verify batches cut their key tiles into equal ranges over the SMs: two
+    long sequences leave each (sequence, kv head) item in about 30 ranges,
+    merged by the range that arrives last.  The arrival counters are left zero,
+    so repeated launches give the same bits."""
+    W = 16
+    c = cases.small_decode_case("vsplit", 21, "bf16", 16, 2, 128, [8000 + W, 3000 + W, W],
+                                q_per_seq=W)
+    g = cases.rng(21)
+    window = {s: (int(c.ctx_lens[s]) - W, cases.bf16_round(cases.normal(g, (2, W, 128))),
+                  cases.bf16_round(cases.normal(g, (2, W, 128)))) for s in range(c.batch)}
+    first = run_case(c, window)
+    assert_close(first, cases.oracle_decode(c, window=window), "bf16", "vsplit")
+    for _ in range(2):
+        assert np.array_equal(run_case(c, window), first)
 
 
 def test_verify_window_ignores_stale_pool_slots():
