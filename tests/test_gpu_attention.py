@@ -92,11 +92,10 @@ def test_verify_window_matches_oracle(hq, hkv, W):
     check(c, window)
 
 
-def test_verify_split_merges_many_ranges_and_repeats():
-    """Verify batches cut their key tiles into equal ranges over the SMs: two
-    long sequences leave each (sequence, kv head) item in about 30 ranges,
-    merged by the range that arrives last.  The arrival counters are left zero,
-    so repeated launches give the same bits."""
+def test_verify_long_windows_repeat_bit_for_bit():
+    """A 16-row verify window over long contexts (GQA 8, so one 128-row tile
+    holds every row of a kv head): the output matches the oracle, and repeated
+    launches give the same bits."""
     W = 16
     c = cases.small_decode_case("vsplit", 21, "bf16", 16, 2, 128, [8000 + W, 3000 + W, W],
                                 q_per_seq=W)
