@@ -121,6 +121,16 @@ MF_DEVINL int length_bucket(int kv_len, int tiles) {
   return NBK - 2 - min(8 * e + mant, NBK - 2);
 }
 
+// Verify items (a window: one query tile per sequence in practice) sort by
+// their exact key-tile count, so the snake deal pairs long and short items
+// as closely as the counts allow; other items by length_bucket.
+template <typename PP>
+MF_DEVINL int sort_bucket(const PP& P, int kv_len, int q_len, int tiles) {
+  if (!P.window || tiles == 0 || kv_len <= 0) return length_bucket(kv_len, tiles);
+  const int nt = (kv_len - q_len + BN - 1) / BN + 1;
+  return NBK - 2 - min(nt, NBK - 2);
+}
+
 // Work item handled by this CTA in its k-th step: items are dealt to the CTAs
 // in a snake order (0..G-1, then G-1..0, ...), so that with the longest items
 // first the CTAs that get the longest of one pass get the shortest of the next.
@@ -257,7 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
         tiles = (ql + ppt - 1) / ppt;
       }
     }
-    atomicAdd(&counts[length_bucket(kvl, tiles)], 1);
+    atomicAdd(&counts[sort_bucket(P, kvl, ql, tiles)], 1);
     prefix[i + 1] = tiles;
   }
   __syncthreads();
@@ -279,7 +289,9 @@ __global__ void __launch_bounds__(THREADS, 1) prefill_kernel(
   if (warp == 0) {  // place the sequences 32 at a time, in index order
     for (int c0 = 0; c0 < B; c0 += 32) {
       const int i = c0 + lane;
-      const int b = i < B ? length_bucket(P.a.kv_lens[i], prefix[i + 1]) : -1;
+      int qs_, ql_ = 0;
+      if (i < B) seq_rows(P.a, i, qs_, ql_);
+      const int b = i < B ? sort_bucket(P, P.a.kv_lens[i], ql_, prefix[i + 1]) : -1;
       const unsigned same = __match_any_sync(0xffffffffu, b);
       const int slot = b >= 0 ? counts[b] + __popc(same & ((1u << lane) - 1u)) : 0;
       __syncwarp();
