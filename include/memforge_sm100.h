@@ -183,7 +183,9 @@ typedef struct {
 /* Device workspace `mf_paged_attention` needs for these arguments on `device`
  * (0 when none).  The caller allocates it once, ZERO-FILLED, and may reuse it
  * for any later call with an equal or smaller requirement on the same stream:
- * the kernels leave it zeroed.  Concurrent launches must not share one. */
+ * its front holds split-K arrival counters, which every launch leaves zero
+ * again; the rest holds partial results that each launch overwrites before
+ * reading.  Concurrent launches must not share one. */
 MF_API size_t mf_paged_attention_workspace_size(const mf_attention_args* args, int device);
 
 MF_API int mf_paged_attention(const mf_attention_args* args, void* workspace,
