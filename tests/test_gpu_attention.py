@@ -45,7 +45,7 @@ def check(case, window=None):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 4), (28, 4), (32, 8), (64, 8)])
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 4), (28, 4), (32, 8), (64, 8), (8, 1), (16, 2)])
 def test_decode_matches_oracle(hq, hkv, dtype):
     c = cases.small_decode_case(f"dec{hq}x{hkv}", 100 + hq, dtype, hq, hkv, 128, [1, 77, 300])
     check(c)
@@ -61,6 +61,15 @@ def test_ragged_lengths_and_page_boundaries(ctx, D):
 def test_many_way_split_merges_exactly():
     """Few long sequences over 148 SMs: each is cut into ~50-150 ranges."""
     c = cases.small_decode_case("split", 8, "bf16", 32, 8, 128, [4000, 3000, 1, 17])
+    check(c)
+
+
+@pytest.mark.parametrize("hq,hkv", [(8, 1), (16, 2)])
+def test_one_or_two_kv_heads_many_ranges(hq, hkv):
+    """The per-GPU shapes of an 8- or 4-way kv-head shard of a GQA-8 model: the
+    SM runs 8 or 4 independent page ranges, so long sequences are cut into
+    many pieces that merge."""
+    c = cases.small_decode_case(f"few{hkv}", 22, "bf16", hq, hkv, 128, [6000, 2500, 1, 700, 33])
     check(c)
 
 
