@@ -132,8 +132,10 @@ Dispatch plan_dispatch(const AttnParams& p, mf_dtype dtype, int sm_count) {
   const bool window = p.wk != nullptr;
   const int G = p.hq / p.hkv;
   if ((int64_t)G * p.max_q_len > 8 && prefill_tc_unsupported(p, dtype) == nullptr) {
-    if (G > 8) {
-      d.mode = Dispatch::PREFILL;  // no run is short enough for the decode kernel
+    if (G > 8 || !p.cu_q) {
+      // No run is short enough for the decode kernel: G > 8, or every run has
+      // the same q_per_seq rows (no cu_seqlens_q), all of them long.
+      d.mode = Dispatch::PREFILL;
       d.rows_cap = 0;
       return d;
     }
