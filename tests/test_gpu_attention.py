@@ -117,6 +117,39 @@ def test_verify_long_windows_repeat_bit_for_bit():
         assert np.array_equal(run_case(c, window), first)
 
 
+def test_uniform_long_runs_need_no_decode_launch():
+    """A verify batch with one q_per_seq (every run longer than 8 rows per kv
+    head) is served by the tcgen05 kernel alone, so it needs no workspace; a
+    varlen batch that mixes one-row and long runs also launches the decode
+    kernel, which does."""
+    from memforge_b200._lib import MF_EWORKSPACE, MemforgeError
+    W = 5
+    c = cases.small_decode_case("uni", 23, "bf16", 40, 8, 128, [W + 300, W + 40], q_per_seq=W)
+    g = cases.rng(23)
+    window = {s: (int(c.ctx_lens[s]) - W, cases.bf16_round(cases.normal(g, (8, W, 128))),
+                  cases.bf16_round(cases.normal(g, (8, W, 128)))) for s in range(c.batch)}
+    empty = torch.empty(0, dtype=torch.uint8, device="cuda")
+    q = to_dev(c.q, "bf16")
+    out = torch.empty_like(q)
+    kp, vp = to_dev(c.k_pool, "bf16"), to_dev(c.v_pool, "bf16")
+    tables = torch.from_numpy(c.tables.clip(min=0)).cuda()
+    kv = torch.from_numpy(c.ctx_lens).cuda()
+    wk = to_dev(np.concatenate([np.transpose(window[s][1], (1, 0, 2)) for s in range(c.batch)]), "bf16")
+    wv = to_dev(np.concatenate([np.transpose(window[s][2], (1, 0, 2)) for s in range(c.batch)]), "bf16")
+    K.paged_attention(q, out, kp, vp, tables, kv, q_per_seq=W, scale=c.scale, win_k=wk, win_v=wv,
+                      workspace_tensor=empty)
+    torch.cuda.synchronize()
+    K.check_device_errors(q.device)
+    assert_close(to_np32(out), cases.oracle_decode(c, window=window), "bf16", "uniform verify")
+    # the same pool as a varlen batch: a one-row run beside a 40-row run
+    cu = torch.tensor([0, 1, 41], dtype=torch.int32, device="cuda")
+    qv = torch.empty((41, 40, 128), dtype=torch.bfloat16, device="cuda").normal_()
+    with pytest.raises(MemforgeError) as e:
+        K.paged_attention(qv, torch.empty_like(qv), kp, vp, tables, kv, cu_seqlens_q=cu,
+                          max_q_len=40, scale=c.scale, workspace_tensor=empty)
+    assert e.value.code == MF_EWORKSPACE
+
+
 def test_verify_window_ignores_stale_pool_slots():
     """With a side window the pool holds only the context: NaN in its unwritten
     slots (where the window's positions would go) must not leak."""
