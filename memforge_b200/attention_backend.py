@@ -54,11 +54,12 @@ _local = threading.local()
 class _DeviceRows:
     """Kernel metadata of one set of query rows, resident on the device."""
 
-    __slots__ = ("tables", "cu", "kv", "row_map", "max_q", "rows")
+    __slots__ = ("tables", "cu", "kv", "row_map", "max_q", "rows", "q_per_seq")
 
-    def __init__(self, tables, cu, kv, row_map, max_q, rows):
+    def __init__(self, tables, cu, kv, row_map, max_q, rows, q_per_seq=0):
         self.tables, self.cu, self.kv, self.row_map = tables, cu, kv, row_map
         self.max_q, self.rows = max_q, rows
+        self.q_per_seq = q_per_seq  # > 0: every sequence has this many rows, in order
 
 
 def _upload(arrays: List, device) -> List[torch.Tensor]:
@@ -109,7 +110,7 @@ class _Binding:
                                  f"table has {table.numel()} entries")
             tables = table.reshape(1, -1).to(device=device, dtype=torch.int32)
             cu, kv = _upload([[0, q_len], [ctx]], device)
-            meta = _DeviceRows(tables, cu, kv, None, q_len, q_len)
+            meta = _DeviceRows(tables, cu, kv, None, q_len, q_len, q_per_seq=q_len)
             self._meta[key] = meta
         return meta
 
@@ -136,7 +137,8 @@ class _VarlenBinding:
                 len(self.seq_ids), self.block_tables, self.seq_ids, self.positions,
                 self.pool.block_size, num_heads, self.pool.key_pool.shape[3], device)
             tables = _varlen_tables(plan, self.block_tables, index, device)
-            self._meta = _DeviceRows(tables, cu, kv, row_map, plan.max_q_len, plan.total)
+            self._meta = _DeviceRows(tables, cu, kv, row_map, plan.max_q_len, plan.total,
+                                     q_per_seq=plan.uniform_q)
         return self._meta
 
 
@@ -209,9 +211,14 @@ def any_binding_active() -> bool:
 # ------------------------------------------------------------ the function
 
 def _run(query_rows, out_rows, pool, layer_idx, meta: _DeviceRows, scale, causal=True):
-    K.paged_attention(query_rows, out_rows, pool.key_pool[layer_idx], pool.value_pool[layer_idx],
-                      meta.tables, meta.kv, cu_seqlens_q=meta.cu, max_q_len=meta.max_q,
-                      scale=scale, causal=causal, row_map=meta.row_map)
+    if meta.q_per_seq:
+        K.paged_attention(query_rows, out_rows, pool.key_pool[layer_idx],
+                          pool.value_pool[layer_idx], meta.tables, meta.kv,
+                          q_per_seq=meta.q_per_seq, scale=scale, causal=causal)
+    else:
+        K.paged_attention(query_rows, out_rows, pool.key_pool[layer_idx],
+                          pool.value_pool[layer_idx], meta.tables, meta.kv, cu_seqlens_q=meta.cu,
+                          max_q_len=meta.max_q, scale=scale, causal=causal, row_map=meta.row_map)
 
 
 def paged_attention_forward(module: Any, query: torch.Tensor, key: torch.Tensor,

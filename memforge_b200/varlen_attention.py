@@ -100,9 +100,14 @@ def _run(query, key_layer, value_layer, block_tables, seq_ids, positions, scale,
     scale = scale if scale is not None else 1.0 / math.sqrt(head_dim)
     tables = _tables(plan, block_tables, index, query.device)
     out = torch.empty_like(query, memory_format=torch.contiguous_format)
-    K.paged_attention(query[0].transpose(0, 1), out[0].transpose(0, 1), key_layer, value_layer,
-                      tables, kv, cu_seqlens_q=cu, max_q_len=plan.max_q_len, scale=scale,
-                      causal=True, row_map=row_map)
+    if plan.uniform_q:
+        K.paged_attention(query[0].transpose(0, 1), out[0].transpose(0, 1), key_layer,
+                          value_layer, tables, kv, q_per_seq=plan.uniform_q, scale=scale,
+                          causal=True)
+    else:
+        K.paged_attention(query[0].transpose(0, 1), out[0].transpose(0, 1), key_layer,
+                          value_layer, tables, kv, cu_seqlens_q=cu, max_q_len=plan.max_q_len,
+                          scale=scale, causal=True, row_map=row_map)
     return out
 
 

@@ -55,6 +55,19 @@ class VarlenPlan:
         return int(self.kv_lens.shape[0])
 
     @property
+    def uniform_q(self) -> int:
+        """
+        The common query-run length when every segment has the same number of
+        rows and the rows are already in segment order (no row map), else 0.
+        Such a batch is passed as ``q_per_seq``: the attention call then needs
+        no per-segment offsets, and a batch of long runs is one launch.
+        """
+        q = np.diff(self.cu_seqlens)
+        if self.row_map is not None or q.size == 0 or (q != q[0]).any():
+            return 0
+        return int(q[0])
+
+    @property
     def width(self) -> int:
         return max(1, int(self.needed.max()))
 

@@ -91,3 +91,17 @@ def test_planning_reads_table_lengths_only():
             return self.n
     p = plan_varlen(3, [SizedOnly(3), SizedOnly(5)], [1, 1, 0], [8, 9, 2], 4, 4, 2)
     assert p.kv_lens.tolist() == [10, 3] and p.needed.tolist() == [3, 1]
+
+
+def test_uniform_runs_in_order_pass_as_q_per_seq():
+    """Equal runs already in segment order (a speculative verify pass): the
+    plan reports the common length, so the call needs no per-segment offsets."""
+    t = tables(20, 30, 12)
+    p = plan_varlen(9, t, [0, 0, 0, 1, 1, 1, 2, 2, 2],
+                    [17, 18, 19, 27, 28, 29, 9, 10, 11], 4, 8, 2)
+    assert p.row_map is None and p.cu_seqlens.tolist() == [0, 3, 6, 9]
+    assert p.uniform_q == 3
+    # unequal runs, or rows that need a map, keep the varlen form
+    assert plan_varlen(4, tables(20), [0, 0, 0, 0], [3, 4, 9, 10], 4, 4, 4).uniform_q == 2
+    assert plan_varlen(3, tables(20, 12), [0, 0, 1], [8, 9, 11], 4, 4, 2).uniform_q == 0
+    assert plan_varlen(4, tables(11, 6, 20), [1, 0, 2, 0], [5, 9, 19, 10], 4, 8, 2).uniform_q == 0
